@@ -1,0 +1,391 @@
+"""Benchmark of the B200 MLA decode path (one JSON line on stdout, rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+
+A step is one ``mla_decode`` call over one batch of the workload (BASELINE
+config 2 by default: B=32 requests x 4096 cached tokens, H=128, bf16, paged
+cache with 64-token pages, shuffled block table, scale 1/sqrt(192)), inputs
+resident in HBM, L2 flushed (256 MiB write) before every timed step, each step
+timed with CUDA events on the launching stream.
+
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): requests are
+independent, so every rank decodes its own batch from its own page pool; there
+is no collective on the data path (NCCL only for barriers and the max-over-ranks
+timing).  Scaling is weak: per-GPU work is fixed.
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+numpy oracle) on the host cores on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "triton-mla_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MLA decode µs/call and TFLOPS (H=128, bf16, paged) vs roofline at 1/2/4/8 B200"
+D_QK, D_V, PAGE = 576, 512, 64
+SCALE = 192 ** -0.5
+L2_FLUSH_BYTES = 256 << 20
+
+CONFIGS = {
+    "cfg2": dict(desc="BASELINE config 2: B=32 H=128 S=4096 (all requests) page 64 bf16 paged, shuffled pages",
+                 batch=32, seqlen=4096, ragged=False),
+    "cfg3": dict(desc="BASELINE config 3: B=4 H=128 S=65536 page 64 bf16 paged, shuffled pages",
+                 batch=4, seqlen=65536, ragged=False),
+    "cfg4": dict(desc="BASELINE config 4: B=256 H=128 S~U[1,16384] page 64 bf16, pages from one shared pool",
+                 batch=256, seqlen=16384, ragged=True),
+}
+
+
+def decode_flops(total_tokens, heads):
+    """Algorithmic FLOPs of one call: T*H*2*(576+512) (the reference bench's model, bench.py:81)."""
+    return float(total_tokens) * heads * 2 * (D_QK + D_V)
+
+
+def decode_bytes(total_tokens, batch, heads, elt=2):
+    """Algorithmic bytes of one call: cache rows + q + out (bench.py:80 of the reference)."""
+    return float(total_tokens * D_QK + batch * heads * D_QK + batch * heads * D_V) * elt
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def make_workload(cfg, device, seed):
+    import torch
+    gen_cpu = torch.Generator().manual_seed(seed)
+    if cfg["ragged"]:
+        lens = torch.randint(1, cfg["seqlen"] + 1, (cfg["batch"],), generator=gen_cpu, dtype=torch.int32)
+    else:
+        lens = torch.full((cfg["batch"],), cfg["seqlen"], dtype=torch.int32)
+    need = (lens + PAGE - 1) // PAGE
+    num_pages = int(need.sum())
+    g = torch.Generator(device=device).manual_seed(seed)
+    kv = torch.randn(num_pages, PAGE, D_QK, generator=g, device=device, dtype=torch.bfloat16)
+    q = torch.randn(cfg["batch"], 128, D_QK, generator=g, device=device, dtype=torch.bfloat16)
+    perm = torch.randperm(num_pages, generator=gen_cpu)
+    bt = torch.zeros(cfg["batch"], int(need.max()), dtype=torch.int32)
+    at = 0
+    for b, k in enumerate(need.tolist()):
+        bt[b, :k] = perm[at:at + k].int()
+        at += k
+    return q, kv, lens.to(device), bt.to(device)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_oracle_rate(budget_s=10.0, seqlen=4096, heads=128):
+    """The numpy oracle (reference algorithm) on host cores: TFLOPS on whole requests of the workload."""
+    import numpy as np
+    from oracle import mla_oracle as orc
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, heads, D_QK), dtype=np.float32)
+    kv = rng.standard_normal((1, seqlen, D_QK), dtype=np.float32)
+    lens = np.array([seqlen])
+    orc.mla_decode_ref(q, kv, lens, None, softmax_scale=SCALE, dtype=np.float32)  # warm
+    done, t0 = 0, time.perf_counter()
+    while True:
+        orc.mla_decode_ref(q, kv, lens, None, softmax_scale=SCALE, dtype=np.float32)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    flops = decode_flops(seqlen * done, heads)
+    return flops / el / 1e12, done, el
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm's CPU restatement, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import mla_oracle as orc
+    cfg = CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    seqlen = cfg["seqlen"] if not cfg["ragged"] else 8192
+    q = rng.standard_normal((1, 128, D_QK), dtype=np.float32)
+    kv = rng.standard_normal((1, seqlen, D_QK), dtype=np.float32)
+    lens = np.array([seqlen])
+    for _ in range(args.warmup):
+        orc.mla_decode_ref(q, kv, lens, None, softmax_scale=SCALE, dtype=np.float32)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        orc.mla_decode_ref(q, kv, lens, None, softmax_scale=SCALE, dtype=np.float32)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    tflops = decode_flops(seqlen, 128) / (ms * 1e-3) / 1e12
+    sample = f"1 request x {seqlen} tokens x 128 heads per step (fp32 numpy, BLAS threads={threads})"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+        "config": {"workload": cfg["desc"], "sample": sample},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": tflops, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kernel", default="auto", choices=["auto", "sm100", "generic"])
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (rank 0, N=1)")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from triton_mla import _lib, get_num_splits, mla_decode
+    from triton_mla.kernel import _DTYPE_CODES, _KERNELS, _status_word, selected_kernel
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    cfg = CONFIGS[args.config]
+    q, kv, lens, bt = make_workload(cfg, device, seed=1000 + rank)
+    B = q.shape[0]
+    total_tokens = int(lens.sum())
+    flops = decode_flops(total_tokens, 128)
+    nbytes = decode_bytes(total_tokens, B, 128)
+    splits = get_num_splits(B, 128, int(lens.max()), torch.cuda.get_device_properties(device).multi_processor_count)
+    kname = selected_kernel(q, kv, bt, num_splits=splits, kernel=args.kernel)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return mla_decode(q, kv, lens, bt, softmax_scale=SCALE, num_splits=splits, return_lse=True,
+                          kernel=args.kernel)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, L2 flushed before each, events around each step.
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = sum(step_ms) / len(step_ms)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    gpu_launches = args.steps * (1 + (1 if splits > 1 else 0))
+
+    # ---- dominant kernel alone (stage 1 through the C ABI), same stream, same flush discipline.
+    lib = _lib.load()
+    lse = torch.empty(B, 128, dtype=torch.float32, device=device)
+    out = torch.empty(B, 128, D_V, dtype=torch.bfloat16, device=device)
+    ws = torch.empty(max(lib.tmla_workspace_bytes(B, 128, max(splits, 2), D_V), 1), dtype=torch.uint8, device=device)
+    o_bytes = (B * 128 * max(splits, 2) * D_V * 4 + 255) & ~255
+    p = _lib.TmlaDecodeParams(
+        q.data_ptr(), q.stride(0), q.stride(1), kv.data_ptr(), kv.stride(0), kv.stride(1), kv.shape[0], PAGE,
+        lens.data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1], out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr(), lse.stride(0), ws.data_ptr(), ws.data_ptr() + o_bytes, _status_word(device).data_ptr(),
+        B, 128, D_QK, D_V, splits, _DTYPE_CODES[torch.bfloat16], _KERNELS[args.kernel],
+        0 if splits > 1 else _lib.FLAG_PARTIAL_ONLY, SCALE)
+    ks, ke = [], []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        _lib.check(lib.tmla_decode_partial(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "partial")
+        b.record(stream)
+        if i >= args.warmup:
+            ks.append(a)
+            ke.append(b)
+    torch.cuda.synchronize()
+    kern_ms = sum(a.elapsed_time(b) for a, b in zip(ks, ke)) / len(ks)
+
+    # ---- end to end through the public API from pinned host memory.
+    q_h = q.cpu().pin_memory()
+    lens_h = lens.cpu().pin_memory()
+    bt_h = bt.cpu().pin_memory()
+    out_h = torch.empty(B, 128, D_V, dtype=torch.bfloat16).pin_memory()
+    lse_h = torch.empty(B, 128, dtype=torch.float32).pin_memory()
+    h2d = q_h.numel() * 2 + lens_h.numel() * 4 + bt_h.numel() * 4
+    d2h = out_h.numel() * 2 + lse_h.numel() * 4
+
+    def e2e_step():
+        qd = q_h.to(device, non_blocking=True)
+        ld = lens_h.to(device, non_blocking=True)
+        bd = bt_h.to(device, non_blocking=True)
+        o, l = mla_decode(qd, kv, ld, bd, softmax_scale=SCALE, num_splits=splits, return_lse=True,
+                          kernel=args.kernel)
+        out_h.copy_(o, non_blocking=True)
+        lse_h.copy_(l, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_ms = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_step()
+        b.record(stream)
+        b.synchronize()
+        e_ms.append(a.elapsed_time(b))
+    e2e_ms = sum(e_ms) / len(e_ms)
+    te = torch.tensor([e2e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    hbm, tflops_peak, peak_kind = peaks()
+    achieved_gbs = nbytes / (kern_ms * 1e-3) / 1e9
+    achieved_tf = flops / (kern_ms * 1e-3) / 1e12
+    t_bytes = nbytes / (hbm * 1e9)
+    t_flops = flops / (tflops_peak * 1e12)
+    bound = "hbm" if t_bytes >= t_flops else "tensor"
+    roofline = {
+        "bound": bound,
+        "achieved": achieved_gbs if bound == "hbm" else achieved_tf,
+        "peak": hbm if bound == "hbm" else tflops_peak,
+        "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+        "frac": (achieved_gbs / hbm) if bound == "hbm" else (achieved_tf / tflops_peak),
+        "traffic": None,
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
+        "kernel": f"stage 1 ({kname})",
+        "kernel_us": kern_ms * 1e3,
+        "tensor_frac": achieved_tf / tflops_peak,
+        "call_roofline_frac": max(t_bytes, t_flops) / (ms * 1e-3),
+        "algorithmic_bytes_per_launch": nbytes,
+        "algorithmic_flops_per_launch": flops,
+    }
+    cpu = None
+    if world == 1 and args.cpu_budget > 0:
+        rate, done, el = cpu_oracle_rate(args.cpu_budget)
+        cpu = {"value": rate, "unit": "TFLOPS", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{done} requests x 4096 tokens x 128 heads of the workload in {el:.1f}s "
+                         "(numpy oracle, fp32, BLAS threads = all host cores)"}
+    line = {
+        "metric": METRIC,
+        "value": world * flops / (ms_max * 1e-3) / 1e12,
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max,
+        "us_per_call": ms_max * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic N(0,1) (no dataset; BASELINE configs are synthetic)",
+        "config": {"workload": cfg["desc"], "batch_per_gpu": B, "heads": 128, "page_size": PAGE,
+                   "tokens_per_gpu": total_tokens, "num_splits": splits, "kernel": kname,
+                   "l2": "flushed (256 MiB write) before every timed step", "parallelism": f"dp{world} (batch-sharded)"},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "per step: q, seqlens, block_table host->device; out, lse device->host; cache resident"},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,138 @@
+/*
+ * triton_mla_b200.h — C ABI of the B200 (sm_100a) MLA single-token decode library.
+ *
+ * This is the drop-in boundary for the hot path of luvadlamudi/triton-mla.
+ * The reference exposes the path as the Python function
+ * `triton_mla.mla_decode` (src/triton_mla/kernel.py:204-323), which launches
+ * two Triton kernels: `_mla_decode_stage1` (kernel.py:43-138, split-KV partial
+ * attention) and `_mla_decode_stage2` (kernel.py:141-181, log-sum-exp merge),
+ * after picking a split count with `get_num_splits` (kernel.py:190-201).
+ * Each entry point below replaces one of those pieces; the Python package
+ * `triton_mla` (triton-mla_b200/triton_mla/) binds them with ctypes.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  All tensor pointers are DEVICE pointers of
+ *    the current CUDA device; strides are in ELEMENTS; the innermost dimension
+ *    of q, kv_cache and out is contiguous (stride 1), as the reference asserts
+ *    (kernel.py:241).
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Every function returns 0 on success or a TMLA_ERR_* code; nothing is
+ *    allocated or freed by the library except where noted (it never calls
+ *    cudaMalloc).  Launches are asynchronous; device-side faults of the
+ *    input (a block-table entry outside [0, num_pages), a bounded wait that
+ *    timed out) are reported through the optional `status` word, never by
+ *    trapping.
+ */
+#ifndef TRITON_MLA_B200_H
+#define TRITON_MLA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TMLA_ABI_VERSION 1
+
+/* Return codes. */
+#define TMLA_OK 0
+#define TMLA_ERR_INVALID_ARG 1     /* shape / stride / dtype rule broken (reference: AssertionError) */
+#define TMLA_ERR_UNSUPPORTED 2     /* a configuration this build does not implement */
+#define TMLA_ERR_MISALIGNED 3      /* a pointer or stride breaks the 16-byte TMA rule */
+#define TMLA_ERR_CUDA 4            /* a CUDA runtime/driver call failed; see tmla_last_cuda_error() */
+#define TMLA_ERR_WORKSPACE 5       /* workspace missing or too small */
+
+/* Bits of the device status word (OR-ed by kernels). */
+#define TMLA_STATUS_BAD_PAGE 0x1   /* a block-table entry was outside [0, num_pages); its tokens were masked */
+#define TMLA_STATUS_TIMEOUT 0x2    /* a bounded pipeline wait gave up; the result is invalid */
+
+/* Element types of q / kv_cache / out. */
+#define TMLA_DTYPE_BF16 0
+#define TMLA_DTYPE_FP16 1
+#define TMLA_DTYPE_FP32 2          /* generic kernel only */
+
+/* Kernel selection for tmla_decode / tmla_decode_partial. */
+#define TMLA_KERNEL_AUTO 0         /* tcgen05 kernel when the shape allows it, else the generic kernel */
+#define TMLA_KERNEL_GENERIC 1      /* CUDA-core split-KV kernel: any power-of-two head_dim_v / rope dim */
+#define TMLA_KERNEL_SM100 2        /* TMA + tcgen05 + TMEM kernel: d_qk 576, d_v 512, 16-bit types */
+
+/* Flags. */
+#define TMLA_FLAG_PARTIAL_ONLY 0x1  /* write ws_o / ws_lse even when num_splits == 1 (stage-1 semantics) */
+
+typedef struct TmlaDecodeParams {
+  /* q [batch, num_heads, d_qk]: absorbed nope query (first d_v dims) then the RoPE query. */
+  const void* q;
+  int64_t q_stride_b, q_stride_h;
+
+  /* kv_cache: paged [num_pages, page_size, d_qk] when block_table != NULL,
+     otherwise dense [batch, page_size (= capacity), d_qk] with num_pages = batch. */
+  const void* kv;
+  int64_t kv_stride_page, kv_stride_tok;
+  int64_t num_pages;
+  int32_t page_size;
+
+  const int32_t* seqlens;          /* [batch] valid tokens per request */
+  const int32_t* block_table;      /* [batch, bt_width] page ids, or NULL for dense */
+  int64_t bt_stride;               /* row stride of block_table */
+  int32_t bt_width;                /* pages per row (entries beyond are never read) */
+
+  void* out;                       /* [batch, num_heads, d_v] in the q dtype */
+  int64_t out_stride_b, out_stride_h;
+  float* lse;                      /* [batch, num_heads] fp32 natural-log LSE, or NULL */
+  int64_t lse_stride_b;
+
+  /* Split workspace (only read when num_splits > 1):
+     ws_o [batch, num_heads, num_splits, d_v] fp32 partial outputs (normalised),
+     ws_lse [batch, num_heads, num_splits] fp32 base-2 partial LSE. */
+  float* ws_o;
+  float* ws_lse;
+
+  int32_t* status;                 /* optional device status word (TMLA_STATUS_* bits), or NULL */
+
+  int32_t batch, num_heads, d_qk, d_v, num_splits;
+  int32_t dtype;                   /* TMLA_DTYPE_* */
+  int32_t kernel;                  /* TMLA_KERNEL_* */
+  int32_t flags;                   /* TMLA_FLAG_* bits */
+  float softmax_scale;
+} TmlaDecodeParams;
+
+/* Whole decode: partial attention over num_splits KV ranges, then the merge.
+   Replaces `mla_decode` (kernel.py:204-323) after its host-side validation. */
+int tmla_decode(const TmlaDecodeParams* p, void* stream);
+
+/* Stage 1 only: writes ws_o / ws_lse for every (request, head, split).
+   Replaces the `_mla_decode_stage1` launch (kernel.py:276-302). */
+int tmla_decode_partial(const TmlaDecodeParams* p, void* stream);
+
+/* Stage 2 only: merges ws_o / ws_lse into out (q dtype) and lse (natural log).
+   Replaces the `_mla_decode_stage2` launch (kernel.py:303-320). */
+int tmla_combine(const float* ws_o, const float* ws_lse, void* out, int64_t out_stride_b,
+                 int64_t out_stride_h, float* lse, int64_t lse_stride_b, int32_t batch,
+                 int32_t num_heads, int32_t num_splits, int32_t d_v, int32_t dtype, void* stream);
+
+/* Split count for a batch.  Replaces `get_num_splits` (kernel.py:190-201) with
+   a B200 rule keyed on batch, heads, longest request and SM count. */
+int32_t tmla_num_splits(int32_t batch, int32_t num_heads, int32_t max_seqlen, int32_t num_sms);
+
+/* Bytes of split workspace tmla_decode needs (0 when num_splits == 1). */
+size_t tmla_workspace_bytes(int32_t batch, int32_t num_heads, int32_t num_splits, int32_t d_v);
+
+/* Which kernel TMLA_KERNEL_AUTO would choose for these parameters (TMLA_KERNEL_*),
+   or a negative TMLA_ERR_* code if the parameters are invalid. */
+int tmla_select_kernel(const TmlaDecodeParams* p);
+
+/* Human-readable text of a return code; the CUDA error string of the last
+   TMLA_ERR_CUDA on this thread; and the library's ABI version. */
+const char* tmla_error_string(int code);
+const char* tmla_last_cuda_error(void);
+int tmla_abi_version(void);
+
+/* sizeof(TmlaDecodeParams) as compiled, so an FFI binding can check its mirror of the struct. */
+size_t tmla_params_bytes(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRITON_MLA_B200_H */

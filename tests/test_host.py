@@ -1,0 +1,138 @@
+"""Host-side checks that need no GPU: the C library loads and exports every
+symbol the header declares, the ctypes mirror matches the C struct, argument
+validation and kernel selection, the split heuristic, and the Python wrapper's
+drop-in error behaviour (kernel.py:235-245 of the reference)."""
+
+import ctypes
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+from triton_mla import _lib, get_num_splits, mla_decode
+from triton_mla.kernel import selected_kernel
+
+HEADER = ROOT / "include" / "triton_mla_b200.h"
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.load()
+    declared = set(re.findall(r"\b(tmla_[a-z_0-9]+)\s*\(", HEADER.read_text()))
+    assert declared == set(_lib.EXPORTED), declared ^ set(_lib.EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_struct_layout():
+    lib = _lib.load()
+    assert lib.tmla_abi_version() == _lib.ABI_VERSION
+    assert lib.tmla_params_bytes() == ctypes.sizeof(_lib.TmlaDecodeParams)
+    # Header constants match the binding's.
+    text = HEADER.read_text()
+    for name in ("OK", "ERR_INVALID_ARG", "ERR_UNSUPPORTED", "ERR_MISALIGNED", "ERR_CUDA", "ERR_WORKSPACE",
+                 "STATUS_BAD_PAGE", "STATUS_TIMEOUT", "DTYPE_BF16", "DTYPE_FP16", "DTYPE_FP32", "KERNEL_AUTO",
+                 "KERNEL_GENERIC", "KERNEL_SM100", "FLAG_PARTIAL_ONLY"):
+        m = re.search(rf"#define TMLA_{name}\s+(0x[0-9a-fA-F]+|\d+)", text)
+        assert m and int(m.group(1), 0) == getattr(_lib, name), name
+
+
+def test_error_strings():
+    for code in range(6):
+        assert _lib.error_string(code)
+    assert _lib.error_string(99) == "unknown error"
+
+
+def _params(**kw):
+    p = _lib.TmlaDecodeParams()
+    p.q = p.kv = p.seqlens = p.out = 16
+    p.q_stride_b, p.q_stride_h = 128 * 576, 576
+    p.kv_stride_page, p.kv_stride_tok = 64 * 576, 576
+    p.num_pages, p.page_size = 10, 64
+    p.block_table, p.bt_stride, p.bt_width = 16, 4, 4
+    p.out_stride_b, p.out_stride_h = 128 * 512, 512
+    p.batch, p.num_heads, p.d_qk, p.d_v, p.num_splits = 2, 128, 576, 512, 1
+    p.dtype, p.kernel, p.softmax_scale = _lib.DTYPE_BF16, _lib.KERNEL_AUTO, 0.07
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize("bad", [
+    dict(d_v=500), dict(d_qk=512 + 48), dict(d_qk=512), dict(num_heads=0), dict(num_splits=0),
+    dict(batch=-1), dict(dtype=7), dict(page_size=0), dict(q=None), dict(block_table=None, num_pages=3),
+])
+def test_select_kernel_rejects_invalid(bad):
+    rc = _lib.load().tmla_select_kernel(ctypes.byref(_params(**bad)))
+    assert rc == -_lib.ERR_INVALID_ARG
+
+
+def test_select_kernel_needs_workspace_for_splits():
+    rc = _lib.load().tmla_select_kernel(ctypes.byref(_params(num_splits=4)))
+    assert rc == -_lib.ERR_WORKSPACE
+
+
+def test_select_kernel_generic_for_other_dims():
+    lib = _lib.load()
+    assert lib.tmla_select_kernel(ctypes.byref(_params(d_qk=256 + 32, d_v=256))) == _lib.KERNEL_GENERIC
+    assert lib.tmla_select_kernel(ctypes.byref(_params(dtype=_lib.DTYPE_FP32))) == _lib.KERNEL_GENERIC
+    assert lib.tmla_select_kernel(ctypes.byref(_params(kernel=_lib.KERNEL_GENERIC))) == _lib.KERNEL_GENERIC
+
+
+def test_workspace_bytes():
+    lib = _lib.load()
+    assert lib.tmla_workspace_bytes(4, 128, 1, 512) == 0
+    n = lib.tmla_workspace_bytes(4, 128, 3, 512)
+    assert n >= 4 * 128 * 3 * 513 * 4 and n % 256 == 0
+
+
+@pytest.mark.parametrize("batch,heads,seqlen", [(1, 128, 65536), (4, 128, 65536), (32, 128, 4096),
+                                                (128, 128, 8192), (256, 128, 16384), (2, 16, 1024), (1, 16, 1)])
+def test_num_splits_properties(batch, heads, seqlen):
+    s = get_num_splits(batch, heads, seqlen, 148)
+    assert 1 <= s <= 64
+    assert s <= max(-(-seqlen // 128), 1)
+    # A batch that already fills the machine is split at most to even out the last wave.
+    if batch * ((heads + 127) // 128) >= 148:
+        assert s <= 2
+
+
+def test_num_splits_b200_configs():
+    # BASELINE configs on a 148-SM B200: the long-context case splits to about one wave of clusters.
+    s3 = get_num_splits(4, 128, 65536, 148)
+    assert 4 * s3 <= 74 and 4 * s3 >= 60
+    assert get_num_splits(32, 128, 4096, 148) == 2
+    assert get_num_splits(0, 128, 4096, 148) == 1
+
+
+def test_wrapper_assertions_match_reference():
+    q = torch.zeros(2, 16, 576, dtype=torch.bfloat16)
+    kv = torch.zeros(2, 64, 576, dtype=torch.bfloat16)
+    lens = torch.tensor([3, 4], dtype=torch.int32)
+    with pytest.raises(AssertionError):
+        mla_decode(q, torch.zeros(2, 64, 2, 576, dtype=torch.bfloat16), lens)   # kv head dim != 1
+    with pytest.raises(AssertionError):
+        mla_decode(q[0], kv, lens)                                                # q not 3-D
+    with pytest.raises(AssertionError):
+        mla_decode(q, kv[..., :575], lens)                                         # width mismatch
+    with pytest.raises(AssertionError):
+        mla_decode(q, kv, lens, head_dim_v=500)                                    # not a power of two
+    with pytest.raises(AssertionError):
+        mla_decode(q, kv.half(), lens)                                             # dtype mismatch
+    with pytest.raises(AssertionError):
+        mla_decode(q, torch.zeros(3, 64, 576, dtype=torch.bfloat16), lens)        # dense batch mismatch
+    with pytest.raises(AssertionError):
+        mla_decode(q.transpose(1, 2).contiguous().transpose(1, 2), kv, lens)       # inner stride != 1
+
+
+def test_wrapper_refuses_cpu_tensors():
+    q = torch.zeros(2, 16, 576, dtype=torch.bfloat16)
+    kv = torch.zeros(2, 64, 576, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        mla_decode(q, kv, torch.tensor([3, 4], dtype=torch.int32))
+
+
+def test_selected_kernel_reports_generic_for_non_deepseek_dims_on_cpu_tensors():
+    q = torch.zeros(2, 16, 256 + 32, dtype=torch.bfloat16)
+    kv = torch.zeros(2, 64, 256 + 32, dtype=torch.bfloat16)
+    assert selected_kernel(q, kv, head_dim_v=256) == "generic"

@@ -1,0 +1,136 @@
+// Split merge: out[b,h,:] = sum_s w_s * o_s / sum_s w_s with w_s = 2^(lse_s - max lse).
+//
+// Replaces the reference's `_mla_decode_stage2` (src/triton_mla/kernel.py:141-181):
+// same arithmetic (base-2 weights against the split maximum, an all-empty row
+// gives out 0 and lse -inf, the final LSE is converted to natural log), but
+// one warp per (request, head) row with 16-byte loads of the fp32 partials
+// instead of one 4-warp program per row with a serial split loop.
+#include "tmla_common.cuh"
+
+namespace tmla {
+
+constexpr int kCombineWarps = 8;
+
+template <typename T>
+__device__ __forceinline__ void store4(T* dst, float4 v);
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+template <>
+__device__ __forceinline__ void store4<__half>(__half* dst, float4 v) {
+  __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+template <>
+__device__ __forceinline__ void store4<float>(float* dst, float4 v) {
+  *reinterpret_cast<float4*>(dst) = v;
+}
+
+template <typename T>
+__device__ __forceinline__ T cvt1(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 cvt1<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half cvt1<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float cvt1<float>(float v) { return v; }
+
+template <typename T>
+__global__ void __launch_bounds__(kCombineWarps * 32)
+    mla_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
+                       int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S, int DV,
+                       int vec_ok) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * H) return;
+  const int b = (int)(row / H), h = (int)(row - (int64_t)b * H);
+  const float* L = ws_lse + row * S;
+
+  float m = -INFINITY;
+  for (int s = lane; s < S; s += 32) m = fmaxf(m, L[s]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (m == -INFINITY) m = 0.f;
+
+  const float* O = ws_o + row * (int64_t)S * DV;
+  T* dst = out + (int64_t)b * osb + (int64_t)h * osh;
+  float wsum = 0.f;
+  if (vec_ok) {
+    // DV % 128 == 0: lane owns float4 columns 4*lane + 128*k.
+    const int nk = DV / 128;  // <= 8 for DV <= 1024
+    float4 acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < S; ++s) {
+      const float w = exp2f(L[s] - m);
+      wsum += w;
+      if (w == 0.f) continue;
+      const float4* src = reinterpret_cast<const float4*>(O + (int64_t)s * DV) + lane;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < nk) {
+          float4 v = __ldg(src + k * 32);
+          acc[k].x = fmaf(w, v.x, acc[k].x);
+          acc[k].y = fmaf(w, v.y, acc[k].y);
+          acc[k].z = fmaf(w, v.z, acc[k].z);
+          acc[k].w = fmaf(w, v.w, acc[k].w);
+        }
+      }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < nk) {
+        float4 v = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
+        store4<T>(dst + 4 * lane + 128 * k, v);
+      }
+    }
+  } else {
+    for (int s = 0; s < S; ++s) wsum += exp2f(L[s] - m);
+    const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
+    for (int d = lane; d < DV; d += 32) {
+      float a = 0.f;
+      for (int s = 0; s < S; ++s) a = fmaf(exp2f(L[s] - m), O[(int64_t)s * DV + d], a);
+      dst[d] = cvt1<T>(a * inv);
+    }
+  }
+  if (lse && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+}
+
+template <typename T>
+static int launch_combine_t(const float* ws_o, const float* ws_lse, void* out, int64_t osb, int64_t osh, float* lse,
+                            int64_t lsb, int B, int H, int S, int DV, cudaStream_t stream) {
+  const int64_t rows = (int64_t)B * H;
+  if (rows == 0) return 0;
+  int vec_ok = (DV % 128 == 0) && (DV <= 1024) && (osb % 4 == 0) && (osh % 4 == 0) &&
+               (((uintptr_t)out) % (4 * sizeof(T)) == 0) && (((uintptr_t)ws_o) % 16 == 0);
+  const unsigned grid = (unsigned)((rows + kCombineWarps - 1) / kCombineWarps);
+  mla_combine_kernel<T><<<grid, kCombineWarps * 32, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), osb, osh, lse,
+                                                                 lsb, B, H, S, DV, vec_ok);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -(int)e;
+}
+
+int launch_combine(const float* ws_o, const float* ws_lse, void* out, int64_t osb, int64_t osh, float* lse,
+                   int64_t lsb, int B, int H, int S, int DV, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case TMLA_DTYPE_BF16:
+      return launch_combine_t<__nv_bfloat16>(ws_o, ws_lse, out, osb, osh, lse, lsb, B, H, S, DV, stream);
+    case TMLA_DTYPE_FP16:
+      return launch_combine_t<__half>(ws_o, ws_lse, out, osb, osh, lse, lsb, B, H, S, DV, stream);
+    case TMLA_DTYPE_FP32:
+      return launch_combine_t<float>(ws_o, ws_lse, out, osb, osh, lse, lsb, B, H, S, DV, stream);
+    default:
+      return TMLA_ERR_INVALID_ARG;
+  }
+}
+
+}  // namespace tmla

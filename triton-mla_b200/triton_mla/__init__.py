@@ -1,0 +1,23 @@
+"""triton_mla (B200-native): drop-in replacement for luvadlamudi/triton-mla.
+
+Exports the same names as the reference package (src/triton_mla/__init__.py:1-14).
+``mla_decode`` and ``MLA.forward`` run hand-written sm_100a CUDA kernels from
+``libtriton_mla_b200.so``; there is no Triton and no CPU implementation.
+"""
+
+from .kernel import get_num_splits, mla_decode, read_status, selected_kernel
+from .model import MLA, MLAConfig
+from .reference import mla_decode_ref, mla_decode_torch
+
+__version__ = "0.1.1"
+
+__all__ = [
+    "MLA",
+    "MLAConfig",
+    "get_num_splits",
+    "mla_decode",
+    "mla_decode_ref",
+    "mla_decode_torch",
+    "read_status",
+    "selected_kernel",
+]

@@ -1,0 +1,154 @@
+"""ctypes binding of the C ABI in ``include/triton_mla_b200.h``.
+
+The shared library ``libtriton_mla_b200.so`` (built by ``triton-mla_b200/build.py``)
+holds every CUDA kernel of the package.  There is no other implementation: if
+the library is missing, importing the decode path raises, and a non-CUDA
+tensor raises before any launch.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_NAME = "libtriton_mla_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+ABI_VERSION = 1
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_UNSUPPORTED = 2
+ERR_MISALIGNED = 3
+ERR_CUDA = 4
+ERR_WORKSPACE = 5
+
+STATUS_BAD_PAGE = 0x1
+STATUS_TIMEOUT = 0x2
+
+DTYPE_BF16 = 0
+DTYPE_FP16 = 1
+DTYPE_FP32 = 2
+
+KERNEL_AUTO = 0
+KERNEL_GENERIC = 1
+KERNEL_SM100 = 2
+
+FLAG_PARTIAL_ONLY = 0x1
+
+# Every symbol the header declares; tests check the library exports all of them.
+EXPORTED = (
+    "tmla_decode",
+    "tmla_decode_partial",
+    "tmla_combine",
+    "tmla_num_splits",
+    "tmla_workspace_bytes",
+    "tmla_select_kernel",
+    "tmla_error_string",
+    "tmla_last_cuda_error",
+    "tmla_abi_version",
+    "tmla_params_bytes",
+)
+
+
+class TmlaDecodeParams(ctypes.Structure):
+    """Mirror of ``TmlaDecodeParams`` (field order and types must match the header)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("q_stride_b", ctypes.c_int64),
+        ("q_stride_h", ctypes.c_int64),
+        ("kv", ctypes.c_void_p),
+        ("kv_stride_page", ctypes.c_int64),
+        ("kv_stride_tok", ctypes.c_int64),
+        ("num_pages", ctypes.c_int64),
+        ("page_size", ctypes.c_int32),
+        ("seqlens", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("bt_stride", ctypes.c_int64),
+        ("bt_width", ctypes.c_int32),
+        ("out", ctypes.c_void_p),
+        ("out_stride_b", ctypes.c_int64),
+        ("out_stride_h", ctypes.c_int64),
+        ("lse", ctypes.c_void_p),
+        ("lse_stride_b", ctypes.c_int64),
+        ("ws_o", ctypes.c_void_p),
+        ("ws_lse", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("d_qk", ctypes.c_int32),
+        ("d_v", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("softmax_scale", ctypes.c_float),
+    ]
+
+
+class LibraryError(RuntimeError):
+    """A non-zero return code from the C ABI."""
+
+    def __init__(self, code: int, what: str, detail: str = ""):
+        self.code = code
+        msg = f"{what} failed: {error_string(code)}"
+        if detail:
+            msg += f" ({detail})"
+        super().__init__(msg)
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and type the library; raise loudly if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("TRITON_MLA_LIB", LIB_PATH))
+    if not path.exists():
+        raise ImportError(
+            f"{path} is missing: build the CUDA library with `python triton-mla_b200/build.py` "
+            "(there is no non-CUDA implementation of the decode path)")
+    lib = ctypes.CDLL(str(path))
+    P = ctypes.POINTER(TmlaDecodeParams)
+    i32, i64, vp, f32p = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p
+    lib.tmla_decode.argtypes = [P, vp]
+    lib.tmla_decode.restype = ctypes.c_int
+    lib.tmla_decode_partial.argtypes = [P, vp]
+    lib.tmla_decode_partial.restype = ctypes.c_int
+    lib.tmla_combine.argtypes = [f32p, f32p, vp, i64, i64, f32p, i64, i32, i32, i32, i32, i32, vp]
+    lib.tmla_combine.restype = ctypes.c_int
+    lib.tmla_num_splits.argtypes = [i32, i32, i32, i32]
+    lib.tmla_num_splits.restype = i32
+    lib.tmla_workspace_bytes.argtypes = [i32, i32, i32, i32]
+    lib.tmla_workspace_bytes.restype = ctypes.c_size_t
+    lib.tmla_select_kernel.argtypes = [P]
+    lib.tmla_select_kernel.restype = ctypes.c_int
+    lib.tmla_error_string.argtypes = [ctypes.c_int]
+    lib.tmla_error_string.restype = ctypes.c_char_p
+    lib.tmla_last_cuda_error.argtypes = []
+    lib.tmla_last_cuda_error.restype = ctypes.c_char_p
+    lib.tmla_abi_version.argtypes = []
+    lib.tmla_abi_version.restype = ctypes.c_int
+    lib.tmla_params_bytes.argtypes = []
+    lib.tmla_params_bytes.restype = ctypes.c_size_t
+    if lib.tmla_abi_version() != ABI_VERSION:
+        raise ImportError(f"{path}: ABI version {lib.tmla_abi_version()} != {ABI_VERSION}; rebuild it")
+    if lib.tmla_params_bytes() != ctypes.sizeof(TmlaDecodeParams):
+        raise ImportError("TmlaDecodeParams layout of the library and of the binding differ; rebuild it")
+    _lib = lib
+    return lib
+
+
+def error_string(code: int) -> str:
+    return load().tmla_error_string(code).decode()
+
+
+def check(code: int, what: str) -> None:
+    if code == OK:
+        return
+    detail = load().tmla_last_cuda_error().decode() if code == ERR_CUDA else ""
+    raise LibraryError(code, what, detail)

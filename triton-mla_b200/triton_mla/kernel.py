@@ -1,0 +1,252 @@
+"""Host wrapper of the B200 MLA decode kernels: the drop-in ``mla_decode``.
+
+Same signature, argument meaning, defaults and error behaviour as the
+reference's ``triton_mla.mla_decode`` (src/triton_mla/kernel.py:204-323):
+
+* a 4-D ``[N, P, 1, D]`` cache (FlashMLA layout) is squeezed (kernel.py:235-237);
+* the same ``AssertionError`` checks on ranks, widths, unit inner strides,
+  power-of-two ``head_dim_v`` / RoPE width and equal dtypes (kernel.py:238-245);
+* ``softmax_scale`` defaults to ``d_qk ** -0.5`` (kernel.py:247-248);
+* ``block_table is None`` selects the dense ``[B, S_max, D]`` layout (kernel.py:257-262);
+* ``num_splits=None`` costs one host sync to read the longest request
+  (kernel.py:264-266); an explicit value keeps the call sync-free (CUDA-graph safe);
+* returns ``out [B, H, head_dim_v]`` in ``q.dtype`` and, with ``return_lse``,
+  the natural-log LSE ``[B, H]`` fp32; zero-length requests give 0 and -inf.
+
+Underneath, everything runs in the CUDA library through its C ABI
+(``include/triton_mla_b200.h``); non-CUDA tensors raise ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16, torch.float32: _lib.DTYPE_FP32}
+_KERNELS = {"auto": _lib.KERNEL_AUTO, "generic": _lib.KERNEL_GENERIC, "sm100": _lib.KERNEL_SM100}
+
+B200_NUM_SMS = 148
+
+
+def _is_pow2(v: int) -> bool:
+    return v > 0 and (v & (v - 1)) == 0
+
+
+def _num_sms(device) -> int:
+    """SM count of ``device`` (148 on B200); B200's count when not on CUDA."""
+    if device.type == "cuda":
+        return torch.cuda.get_device_properties(device).multi_processor_count
+    return B200_NUM_SMS
+
+
+def get_num_splits(batch, num_heads, max_seqlen, num_sms, min_tokens_per_split=128):
+    """Split count for one decode call on B200.
+
+    Replaces the reference's one-wave power-of-two rule (kernel.py:190-201).
+    The tcgen05 kernel runs one 2-SM cluster per (request, 128-head tile,
+    split), so a 148-SM B200 holds 74 of them per wave; the C library picks the
+    count that minimises waves x (rows per split + fixed cost) + the fp32
+    partial traffic of the merge.  ``min_tokens_per_split`` caps the count as
+    in the reference.
+    """
+    if batch <= 0 or max_seqlen <= 0:
+        return 1
+    s = int(_lib.load().tmla_num_splits(int(batch), int(num_heads), int(max_seqlen), int(num_sms)))
+    cap = max(-(-int(max_seqlen) // int(min_tokens_per_split)), 1)
+    return max(1, min(s, cap))
+
+
+# ----------------------------------------------------------------------------- device status word
+_status = {}
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    t = _status.get(device.index)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _status[device.index] = t
+    return t
+
+
+def read_status(device=None, reset: bool = True) -> int:
+    """Read (and by default clear) the device status word of ``device``.
+
+    Bits: ``_lib.STATUS_BAD_PAGE`` (a block-table entry outside the page pool
+    or a length beyond the cache; those tokens were masked) and
+    ``_lib.STATUS_TIMEOUT`` (a bounded pipeline wait gave up).  Synchronises.
+    """
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    t = _status_word(device)
+    v = int(t.item())
+    if reset and v:
+        t.zero_()
+    return v
+
+
+_CHECK = os.environ.get("TRITON_MLA_CHECK", "0") == "1"
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "triton_mla (B200) runs only on CUDA tensors; there is no CPU implementation "
+                f"(got a tensor on {t.device})")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def mla_decode(
+    q: torch.Tensor,
+    kv_cache: torch.Tensor,
+    cache_seqlens: torch.Tensor,
+    block_table: torch.Tensor = None,
+    head_dim_v: int = 512,
+    softmax_scale: float = None,
+    num_splits: int = None,
+    return_lse: bool = False,
+    *,
+    kernel: str = "auto",
+    out: torch.Tensor = None,
+):
+    """Weight-absorbed MLA decode attention over a shared latent KV cache.
+
+    Args:
+        q: [batch, num_heads, head_dim_v + rope_dim]; the first head_dim_v dims
+            are the W_UK-absorbed nope query, the rest the RoPE query.
+        kv_cache: paged [num_blocks, page_size, D] when block_table is given,
+            otherwise contiguous [batch, max_seqlen, D]; [..., 1, D] accepted.
+        cache_seqlens: [batch] number of valid tokens per sequence.
+        block_table: optional [batch, max_blocks_per_seq] page indices.
+        head_dim_v: latent rank (512 for DeepSeek-V2/V3).
+        softmax_scale: defaults to q.shape[-1] ** -0.5.
+        num_splits: KV splits; None picks one (one host sync); pass it
+            explicitly for CUDA-graph capture.
+        return_lse: also return the natural-log log-sum-exp per head.
+        kernel: keyword-only, "auto" (tcgen05 kernel where the shape allows),
+            "sm100" (require it) or "generic" (CUDA-core kernel).
+        out: keyword-only preallocated [batch, num_heads, head_dim_v] output.
+
+    Returns:
+        out [batch, num_heads, head_dim_v] (and lse [batch, num_heads] fp32).
+    """
+    if kv_cache.dim() == 4:
+        assert kv_cache.shape[2] == 1, "MLA uses a single shared latent KV head"
+        kv_cache = kv_cache.squeeze(2)
+    assert q.dim() == 3 and kv_cache.dim() == 3
+    batch, num_heads, d_qk = q.shape
+    d_rope = d_qk - head_dim_v
+    assert kv_cache.shape[-1] == d_qk
+    assert q.stride(-1) == 1 and kv_cache.stride(-1) == 1
+    assert _is_pow2(head_dim_v)
+    assert _is_pow2(d_rope)
+    assert q.dtype == kv_cache.dtype
+    if block_table is None:
+        assert kv_cache.shape[0] == batch
+    _require_cuda(q, kv_cache, cache_seqlens, block_table)
+    if q.dtype not in _DTYPE_CODES:
+        raise TypeError(f"unsupported dtype {q.dtype}; use bfloat16, float16 or float32")
+    if kernel not in _KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
+
+    if softmax_scale is None:
+        softmax_scale = d_qk ** -0.5
+    cache_seqlens = cache_seqlens.to(torch.int32)
+    if cache_seqlens.stride(0) != 1:
+        cache_seqlens = cache_seqlens.contiguous()
+
+    paged = block_table is not None
+    if paged:
+        block_table = block_table.to(torch.int32)
+        if block_table.stride(-1) != 1:
+            block_table = block_table.contiguous()
+        page_size = kv_cache.shape[1]
+        num_pages = kv_cache.shape[0]
+        bt_width = block_table.shape[1]
+        bt_stride = block_table.stride(0)
+    else:
+        assert kv_cache.shape[0] == batch
+        page_size = kv_cache.shape[1]
+        num_pages = batch
+        bt_width = 0
+        bt_stride = 0
+
+    device = q.device
+    if num_splits is None:
+        max_seqlen = int(cache_seqlens.max().item()) if batch > 0 else 0
+        num_splits = get_num_splits(batch, num_heads, max_seqlen, _num_sms(device))
+    num_splits = int(num_splits)
+
+    if out is None:
+        out = torch.empty(batch, num_heads, head_dim_v, dtype=q.dtype, device=device)
+    else:
+        assert out.shape == (batch, num_heads, head_dim_v) and out.dtype == q.dtype and out.stride(-1) == 1
+    lse = torch.empty(batch, num_heads, dtype=torch.float32, device=device)
+    if batch == 0:
+        return (out, lse) if return_lse else out
+
+    lib = _lib.load()
+    ws_bytes = lib.tmla_workspace_bytes(batch, num_heads, num_splits, head_dim_v)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+    ws_o = ws_lse = None
+    if ws is not None:
+        o_bytes = (batch * num_heads * num_splits * head_dim_v * 4 + 255) & ~255
+        ws_o = ws.data_ptr()
+        ws_lse = ws_o + o_bytes
+
+    p = _lib.TmlaDecodeParams(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        kv_cache.data_ptr(), kv_cache.stride(0), kv_cache.stride(1), num_pages, page_size,
+        cache_seqlens.data_ptr(), _ptr(block_table), bt_stride, bt_width,
+        out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr(), lse.stride(0),
+        ws_o, ws_lse, _status_word(device).data_ptr(),
+        batch, num_heads, d_qk, head_dim_v, num_splits,
+        _DTYPE_CODES[q.dtype], _KERNELS[kernel], 0, float(softmax_scale),
+    )
+    prev = torch.cuda.current_device()
+    if prev != device.index:
+        torch.cuda.set_device(device)
+    try:
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.tmla_decode(ctypes.byref(p), ctypes.c_void_p(stream)), "tmla_decode")
+    finally:
+        if prev != device.index:
+            torch.cuda.set_device(prev)
+    if _CHECK:
+        st = read_status(device)
+        if st:
+            raise RuntimeError(f"mla_decode device status 0x{st:x} (bad page id / length, or a wait timed out)")
+    if return_lse:
+        return out, lse
+    return out
+
+
+def selected_kernel(q, kv_cache, block_table=None, head_dim_v=512, num_splits=1, kernel="auto") -> str:
+    """Which kernel ``mla_decode`` runs for these tensors: "sm100" or "generic"."""
+    if kv_cache.dim() == 4:
+        kv_cache = kv_cache.squeeze(2)
+    batch, num_heads, d_qk = q.shape
+    p = _lib.TmlaDecodeParams()
+    p.q, p.q_stride_b, p.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
+    p.kv, p.kv_stride_page, p.kv_stride_tok = kv_cache.data_ptr(), kv_cache.stride(0), kv_cache.stride(1)
+    p.page_size = kv_cache.shape[1]
+    if block_table is not None:
+        p.block_table, p.bt_stride, p.bt_width = block_table.data_ptr(), block_table.stride(0), block_table.shape[1]
+        p.num_pages = kv_cache.shape[0]
+    else:
+        p.num_pages = batch
+    p.seqlens = p.out = 1  # only checked for being non-null
+    p.ws_o = p.ws_lse = 1
+    p.batch, p.num_heads, p.d_qk, p.d_v, p.num_splits = batch, num_heads, d_qk, head_dim_v, num_splits
+    p.dtype, p.kernel = _DTYPE_CODES[q.dtype], _KERNELS[kernel]
+    k = _lib.load().tmla_select_kernel(ctypes.byref(p))
+    if k < 0:
+        raise _lib.LibraryError(-k, "tmla_select_kernel")
+    return {_lib.KERNEL_SM100: "sm100", _lib.KERNEL_GENERIC: "generic"}[k]

@@ -1,0 +1,140 @@
+"""DeepSeek-V2/V3 MLA layer whose decode step runs the B200 decode kernel.
+
+API-compatible with the reference's ``triton_mla.model`` (src/triton_mla/model.py):
+``MLAConfig`` has the same fields, defaults and properties (model.py:13-31);
+``MLA`` has the same parameter names and shapes (``wq_a``, ``q_norm``, ``wq_b``,
+``wkv_a``, ``kv_norm``, ``wkv_b``, ``wo``), so a state dict moves between the two
+unchanged; ``MLA.forward(x, kv_cache, cache_seqlens, block_table=None,
+num_splits=None) -> (out, seqlens)`` appends the new token in place and runs
+the absorbed decode (model.py:101-124); ``MLA.forward_naive`` is the
+decompressed form (model.py:126-144).
+
+The attention step is ``mla_decode`` (CUDA library).  The projections,
+norms, RoPE, cache append and the absorption einsums stay PyTorch (cuBLAS).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .kernel import mla_decode
+from .reference import gather_kv
+
+
+@dataclass
+class MLAConfig:
+    hidden_size: int = 7168
+    num_heads: int = 128
+    q_lora_rank: int = 1536
+    kv_lora_rank: int = 512
+    qk_nope_head_dim: int = 128
+    qk_rope_head_dim: int = 64
+    v_head_dim: int = 128
+    rope_theta: float = 10000.0
+    rms_norm_eps: float = 1e-6
+
+    @property
+    def qk_head_dim(self):
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def kv_cache_dim(self):
+        return self.kv_lora_rank + self.qk_rope_head_dim
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim, eps=1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
+
+
+def apply_rope(x, positions, theta):
+    """Half-split rotary embedding at integer ``positions`` (computed in fp32)."""
+    half = x.shape[-1] // 2
+    exponent = torch.arange(half, device=x.device, dtype=torch.float32) * (2.0 / x.shape[-1])
+    angle = positions.float()[..., None] * theta ** (-exponent)
+    c, s = angle.cos(), angle.sin()
+    a, b = x.float()[..., :half], x.float()[..., half:]
+    return torch.cat([a * c - b * s, b * c + a * s], dim=-1).to(x.dtype)
+
+
+class MLA(nn.Module):
+    """Multi-head Latent Attention; caches only the 512-d latent and the 64-d RoPE key per token."""
+
+    def __init__(self, cfg: MLAConfig):
+        super().__init__()
+        self.cfg = cfg
+        h = cfg.num_heads
+        self.wq_a = nn.Linear(cfg.hidden_size, cfg.q_lora_rank, bias=False)
+        self.q_norm = RMSNorm(cfg.q_lora_rank, cfg.rms_norm_eps)
+        self.wq_b = nn.Linear(cfg.q_lora_rank, h * cfg.qk_head_dim, bias=False)
+        self.wkv_a = nn.Linear(cfg.hidden_size, cfg.kv_cache_dim, bias=False)
+        self.kv_norm = RMSNorm(cfg.kv_lora_rank, cfg.rms_norm_eps)
+        self.wkv_b = nn.Linear(cfg.kv_lora_rank, h * (cfg.qk_nope_head_dim + cfg.v_head_dim), bias=False)
+        self.wo = nn.Linear(h * cfg.v_head_dim, cfg.hidden_size, bias=False)
+        self.softmax_scale = cfg.qk_head_dim ** -0.5
+
+    def _project(self, x, positions):
+        cfg = self.cfg
+        q = self.wq_b(self.q_norm(self.wq_a(x))).view(x.shape[0], cfg.num_heads, cfg.qk_head_dim)
+        q_nope, q_pe = q.split([cfg.qk_nope_head_dim, cfg.qk_rope_head_dim], dim=-1)
+        q_pe = apply_rope(q_pe, positions[:, None], cfg.rope_theta)
+        c_kv, k_pe = self.wkv_a(x).split([cfg.kv_lora_rank, cfg.qk_rope_head_dim], dim=-1)
+        return q_nope, q_pe, self.kv_norm(c_kv), apply_rope(k_pe, positions, cfg.rope_theta)
+
+    @staticmethod
+    def _append_kv(kv_cache, c_kv, k_pe, cache_seqlens, block_table):
+        row = torch.cat([c_kv, k_pe], dim=-1).to(kv_cache.dtype)
+        pos = cache_seqlens.long()
+        req = torch.arange(pos.shape[0], device=pos.device)
+        if kv_cache.dim() == 4:
+            kv_cache = kv_cache.squeeze(2)
+        if block_table is None:
+            kv_cache[req, pos] = row
+        else:
+            page = kv_cache.shape[1]
+            kv_cache[block_table[req, pos // page].long(), pos % page] = row
+
+    def _wkv_b(self):
+        cfg = self.cfg
+        w = self.wkv_b.weight.view(cfg.num_heads, cfg.qk_nope_head_dim + cfg.v_head_dim, cfg.kv_lora_rank)
+        return w[:, : cfg.qk_nope_head_dim], w[:, cfg.qk_nope_head_dim:]
+
+    def forward(self, x, kv_cache, cache_seqlens, block_table=None, num_splits=None):
+        """One decode step for x [batch, hidden]; returns (out [batch, hidden], cache_seqlens + 1)."""
+        q_nope, q_pe, c_kv, k_pe = self._project(x, cache_seqlens)
+        self._append_kv(kv_cache, c_kv, k_pe, cache_seqlens, block_table)
+        seqlens = cache_seqlens + 1
+        w_uk, w_uv = self._wkv_b()
+        q_abs = torch.einsum("bhd,hdc->bhc", q_nope, w_uk)
+        q = torch.cat([q_abs, q_pe], dim=-1).to(kv_cache.dtype).contiguous()
+        o = mla_decode(q, kv_cache, seqlens, block_table, head_dim_v=self.cfg.kv_lora_rank,
+                       softmax_scale=self.softmax_scale, num_splits=num_splits)
+        o = torch.einsum("bhc,hdc->bhd", o.to(w_uv.dtype), w_uv)
+        return self.wo(o.flatten(1)), seqlens
+
+    def forward_naive(self, x, kv_cache, cache_seqlens, block_table=None):
+        """The same decode step without absorption: per-head K/V decompressed from the cache."""
+        cfg = self.cfg
+        q_nope, q_pe, c_kv, k_pe = self._project(x, cache_seqlens)
+        self._append_kv(kv_cache, c_kv, k_pe, cache_seqlens, block_table)
+        seqlens = cache_seqlens + 1
+        kv = gather_kv(kv_cache, seqlens, block_table).to(x.dtype)
+        latent, kpe = kv.split([cfg.kv_lora_rank, cfg.qk_rope_head_dim], dim=-1)
+        kvb = self.wkv_b(latent).view(*latent.shape[:2], cfg.num_heads, -1)
+        k_nope, v = kvb.split([cfg.qk_nope_head_dim, cfg.v_head_dim], dim=-1)
+        k = torch.cat([k_nope, kpe[:, :, None].expand(-1, -1, cfg.num_heads, -1)], dim=-1)
+        q = torch.cat([q_nope, q_pe], dim=-1)
+        logits = torch.einsum("bhd,bshd->bhs", q.float(), k.float()) * self.softmax_scale
+        invalid = torch.arange(kv.shape[1], device=x.device)[None, :] >= seqlens[:, None]
+        probs = logits.masked_fill(invalid[:, None, :], float("-inf")).softmax(-1)
+        o = torch.einsum("bhs,bshd->bhd", probs, v.float()).to(x.dtype)
+        return self.wo(o.flatten(1)), seqlens
