@@ -79,7 +79,7 @@ def test_deepseek_v3_layer_step_against_oracle(device):
     kv_before = kv.float().cpu().numpy()
     with torch.no_grad():
         out, _ = model(x, kv, lens, bt)
-    w = {n: getattr(model, n).weight.float().cpu().double().numpy() for n in recipes.LAYER_PARAM_ORDER}
+    w = {n: getattr(model, n).weight.detach().double().cpu().numpy() for n in recipes.LAYER_PARAM_ORDER}
     c = dict(hidden_size=cfg.hidden_size, num_heads=cfg.num_heads, q_lora_rank=cfg.q_lora_rank,
              kv_lora_rank=cfg.kv_lora_rank, qk_nope_head_dim=cfg.qk_nope_head_dim,
              qk_rope_head_dim=cfg.qk_rope_head_dim, v_head_dim=cfg.v_head_dim, rope_theta=cfg.rope_theta,
