@@ -283,5 +283,10 @@ def test_constant_cache_returns_the_row(device):
 
 def test_kernel_selection_for_deepseek_shape(device):
     q, kv, lens, bt = _baseline_case("cfg2", device)
-    assert selected_kernel(q, kv, bt) in ("sm100", "generic")
+    assert selected_kernel(q, kv, bt) == "sm100"
     assert selected_kernel(q, kv, bt, kernel="generic") == "generic"
+    # Page sizes whose largest power-of-two factor is below 8 go to the generic kernel.
+    kv3 = torch.zeros(10, 3, 576, dtype=torch.bfloat16, device=device)
+    bt3 = torch.zeros(2, 4, dtype=torch.int32, device=device)
+    assert selected_kernel(q[:2], kv3, bt3) == "generic"
+    assert selected_kernel(q[:2].float(), kv3.float(), bt3) == "generic"

@@ -242,8 +242,8 @@ def selected_kernel(q, kv_cache, block_table=None, head_dim_v=512, num_splits=1,
         p.num_pages = kv_cache.shape[0]
     else:
         p.num_pages = batch
-    p.seqlens = p.out = 1  # only checked for being non-null
-    p.ws_o = p.ws_lse = 1
+    p.seqlens = p.out = p.ws_o = p.ws_lse = 256  # only checked for being non-null and aligned
+    p.out_stride_b, p.out_stride_h = num_heads * head_dim_v, head_dim_v
     p.batch, p.num_heads, p.d_qk, p.d_v, p.num_splits = batch, num_heads, d_qk, head_dim_v, num_splits
     p.dtype, p.kernel = _DTYPE_CODES[q.dtype], _KERNELS[kernel]
     k = _lib.load().tmla_select_kernel(ctypes.byref(p))
