@@ -15,11 +15,12 @@
 //   O[:, 256r:256r+256] for all 128 heads in TMEM.
 //   * QK: each CTA computes a partial S = Q_r . K_r^T (128 heads x 64 tokens,
 //     fp32) into one of two TMEM score buffers.
-//   * Softmax rows are split too: CTA r owns heads [64r, 64r+64).  Each CTA
+//   * Softmax rows are split too.  Within each 32-lane TMEM quarter q the
+//     sixteen lanes 32q + 16r + [0,16) are the heads CTA r owns.  Each CTA
 //     sends the partial score rows of the heads it does not own to the peer
 //     (16 KB per tile over distributed shared memory); the owner adds them to
 //     its own partial, runs the online softmax and sends the 16-bit P rows
-//     (8 KB) and the rescale factor back, so both CTAs hold the same P for all
+//     (8 KB) and the rescale factors back, so both CTAs hold the same P for all
 //     128 heads in one of two TMEM P buffers.
 //   * PV: each CTA accumulates O_r += P . V_r with V_r the latent half of the
 //     tile it already holds: the cache is read from HBM once and no MMA is
@@ -32,14 +33,18 @@
 // S0 64 | S1 64 | P0 32 | P1 32.  Q latent dims [128,256) of the half and the
 // RoPE half sit in shared memory (A operand of the remaining K steps).
 //
-// Warp roles (352 threads).  warp 0: TMA producer (block table -> page
-// coordinates); warp 1: TMEM allocation and QK issue; warp 10: PV issue;
-// warps 2-9 are two groups of four (warp w reaches TMEM lanes
-// 32*(w%4)..+31, lane == head):
-//   own heads, both groups   softmax, 32 of the 64 score columns each
-//   peer's heads, group X    score sender: ship the partial rows to the owner
-//   peer's heads, group Y    P receiver: write the owner's P into TMEM, rescale O
-// O is rescaled lazily: only when a row maximum grows by more than 2^8.
+// Warp roles (512 threads).  warp 0: TMA producer (block table -> page
+// coordinates); warp 1: TMEM allocation and QK issue; warp 2: PV issue;
+// warp 3: forwards "buffer read" signals to the peer.
+// Warps 4-15 work on TMEM lane quarter w % 4 (the only lanes a warp can reach),
+// one warp of each role per quarter, so every SM sub-partition runs one
+// softmax warp:
+//   warps 4-7    softmax of the 16 owned rows (4 threads per row, 16-lane TMEM
+//                access shapes), P and rescale factors to the peer
+//   warps 8-11   score senders: ship the peer-owned partial rows to the owner
+//   warps 12-15  P receivers: write the owner's P rows into TMEM, rescale O
+// O is rescaled lazily: only when a row maximum grows by more than 2^8.  The
+// output is written by warps 4-11, one thread per row.
 //
 // Every wait is bounded (2 s per wait, %globaltimer); on expiry the CTA sets
 // TMLA_STATUS_TIMEOUT, all roles leave their loops, in-flight copies and MMAs
@@ -53,11 +58,26 @@
 namespace tmla {
 namespace sm100 {
 
+// Timeline instrumentation (off unless built with -DTMLA_TRACE_ENABLED): %globaltimer
+// stamps of pipeline events of the first CTA, read back with tmla_trace_copy().
+#ifdef TMLA_TRACE_ENABLED
+__device__ unsigned long long g_trace[16 * 256];
+#define TMLA_TRACE_IF(cond, k, j)                                                                         \
+  do {                                                                                                    \
+    if (tracing && (cond) && lane == 0 && (j) < 256) g_trace[(k) * 256 + (j)] = tmla::ptx::globaltimer(); \
+  } while (0)
+#else
+#define TMLA_TRACE_IF(cond, k, j) \
+  do {                            \
+  } while (0)
+#endif
+#define TMLA_TRACE(k, j) TMLA_TRACE_IF(true, k, j)
+
 using namespace ptx;
 
 constexpr int kTile = 64;                 // tokens per pipeline stage
 constexpr int kStages = 4;                // cache-tile ring depth
-constexpr int kThreads = 352;
+constexpr int kThreads = 512;
 constexpr int kHalfLatent = 256;          // latent columns per CTA
 constexpr int kHalfRope = 32;             // RoPE columns per CTA
 constexpr uint32_t kBoxBytes = kTile * 128;                 // one 64-token x 64-dim swizzled box
@@ -70,7 +90,7 @@ constexpr uint32_t kSinBytes = 64 * kTile * 4;              // 16384: peer's par
 constexpr uint32_t kPinBytes = 64 * kTile * 2;              // 8192: owner's P for the peer's 64 heads
 constexpr uint32_t kAlphaBytes = 64 * 4;                    // rescale factors that come with P
 constexpr uint32_t kFinBytes = 64 * 8;                      // final (l, m) of the peer's heads
-constexpr uint32_t kMaxBufBytes = 2048;  // row-max swap [tile parity][own quarter][half][lane], then row sums
+constexpr uint32_t kStatBytes = 128 * 8;  // final (l, m) of all 128 rows for the epilogue
 
 constexpr uint32_t kOffStages = 0;
 constexpr uint32_t kOffQLat = kOffStages + kStages * kStageBytes;
@@ -79,9 +99,9 @@ constexpr uint32_t kOffSin = kOffQRope + kQRopeBytes;
 constexpr uint32_t kOffPin = kOffSin + kSinBytes;
 constexpr uint32_t kOffAlpha = kOffPin + kPinBytes;
 constexpr uint32_t kOffFin = kOffAlpha + kAlphaBytes;
-constexpr uint32_t kOffMax = kOffFin + kFinBytes;
-constexpr uint32_t kOffBar = kOffMax + kMaxBufBytes;
-constexpr uint32_t kNumBars = 2 * kStages + 18;
+constexpr uint32_t kOffStat = kOffFin + kFinBytes;
+constexpr uint32_t kOffBar = kOffStat + kStatBytes;
+constexpr uint32_t kNumBars = 2 * kStages + 19;
 constexpr uint32_t kOffMisc = kOffBar + ((kNumBars * 8 + 63) / 64) * 64;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
@@ -92,7 +112,8 @@ constexpr uint32_t kColP = 448;   // + 32 * buffer
 
 constexpr int kWarpProducer = 0;
 constexpr int kWarpQK = 1;
-constexpr int kWarpPV = 10;
+constexpr int kWarpPV = 2;
+constexpr int kWarpRelay = 3;
 
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 between rescales
@@ -117,8 +138,9 @@ enum : uint32_t {
   kBarFinFull,     // owner's final (l, m) of the peer's heads landed
   kBarDrainQK,
   kBarDrainPV,
-  kBarHalf0,       // the two softmax warps of own quarter 0 / 1 swap row maxima (and sums)
-  kBarHalf1,
+  kBarStats,       // every row's final (l, m) is in shared memory for the epilogue
+  kBarSinRead,     // my softmax warps have read Sin (forwarded to the peer's SoutEmpty)
+  kBarPinRead,     // my P receivers have read Pin (forwarded to the peer's PoutEmpty)
 };
 
 struct Shared {
@@ -173,16 +195,17 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool fp16) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// O[row, c0:c0+32*n] *= alpha for this warp's lanes, in place in TMEM.
-__device__ __forceinline__ void rescale_o(uint32_t t_row, int c0, int nchunks, float alpha) {
+// O[r, :] *= alpha_r for the 16 TMEM lanes at `lanes` (256 fp32 columns, in place):
+// thread t scales lane t/4 by alpha_a and lane t/4 + 8 by alpha_b.
+__device__ __forceinline__ void rescale_rows16(uint32_t lanes, float alpha_a, float alpha_b) {
 #pragma unroll 1
-  for (int c = 0; c < nchunks; ++c) {
+  for (int c = 0; c < 4; ++c) {
     uint32_t o[32];
-    tmem_ld32(t_row + kColO + c0 + 32 * c, o);
+    tmem_ld16x256_x8(lanes + kColO + 64 * c, o);
     tc_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-    tmem_st32(t_row + kColO + c0 + 32 * c, o);
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * ((i & 2) ? alpha_b : alpha_a));
+    tmem_st16x256_x8(lanes + kColO + 64 * c, o);
   }
   tc_wait_st();
 }
@@ -265,6 +288,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int split = blockIdx.y, b = blockIdx.z;
   const int H = p.num_heads;
   Waiter waiter{abort_flag, p.status};
+#ifdef TMLA_TRACE_ENABLED
+  const bool tracing = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  if (tracing && threadIdx.x == 0) g_trace[15 * 256] = globaltimer();
+#endif
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -275,19 +302,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(sh.bar(kBarSFull0 + i), 1);
-      mbar_init(sh.bar(kBarSEmpty0 + i), 6);
-      mbar_init(sh.bar(kBarPFull0 + i), 6);
+      mbar_init(sh.bar(kBarSEmpty0 + i), 8);
+      mbar_init(sh.bar(kBarPFull0 + i), 8);
       mbar_init(sh.bar(kBarPvDone0 + i), 1);
     }
     mbar_init(sh.bar(kBarSinFull), 1);
-    mbar_init(sh.bar(kBarSoutEmpty), 4);
+    mbar_init(sh.bar(kBarSoutEmpty), 1);
     mbar_init(sh.bar(kBarPinFull), 1);
-    mbar_init(sh.bar(kBarPoutEmpty), 2);
+    mbar_init(sh.bar(kBarPoutEmpty), 1);
+    mbar_init(sh.bar(kBarSinRead), 4);
+    mbar_init(sh.bar(kBarPinRead), 4);
     mbar_init(sh.bar(kBarFinFull), 1);
     mbar_init(sh.bar(kBarDrainQK), 1);
     mbar_init(sh.bar(kBarDrainPV), 1);
-    mbar_init(sh.bar(kBarHalf0), 2);
-    mbar_init(sh.bar(kBarHalf1), 2);
+    mbar_init(sh.bar(kBarStats), 8);
     fence_mbar_init();
   }
   if (warp == kWarpQK) {
@@ -331,22 +359,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tma_load_3d(sh.base + kOffQRope, &tm_q_rope, sh.bar(kBarQFull), 512 + kHalfRope * rank, h0, b, pol_q);
     }
     // Page id of sub-box `sb` of tile `j` (-1: past the end of the request).
+    // Raw page id of sub-box `sb` of tile `j` (0 when the sub-box is past the end of
+    // the split); read ahead of use, checked by `page_ok` when used.
     auto page_of = [&](int j, int sb) -> int {
       const int t = start + j * kTile + sb * g;
-      if (sb >= nsub || t >= end) return -1;
+      if (sb >= nsub || t >= end || j >= ntiles) return 0;
       if (!p.block_table) return b;
-      int pg = __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size);
-      if (pg < 0 || (int64_t)pg >= p.num_pages) {
+      return __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size);
+    };
+    // Whether sub-box `sb` of tile `j` is inside the split; a page id outside the
+    // pool is reported and replaced by page 0 (its tokens are not trusted).
+    auto page_ok = [&](int j, int sb, int& pg) -> bool {
+      const int t = start + j * kTile + sb * g;
+      if (sb >= nsub || t >= end || j >= ntiles) return false;
+      if (pg < 0 || (int64_t)pg >= (int64_t)(p.block_table ? p.num_pages : p.batch)) {
         if (p.status) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
         pg = 0;
       }
-      return pg;
+      return true;
     };
+    // Page ids are read one iteration before they are needed .
     int pg_next = ntiles > 0 ? page_of(0, lane) : -1;
     int issued = 0;
     for (int j = 0; j < ntiles; ++j) {
-      const int pg = pg_next;
-      pg_next = (j + 1 < ntiles) ? page_of(j + 1, lane) : -1;
+      int pg = pg_next;
+      pg_next = page_of(j + 1, lane);
       const int s = j % kStages;
       bool ok = true;
       if (lane == 0 && j >= kStages) ok = waiter.wait(sh.bar(kBarKvEmpty + s), ((j / kStages) - 1) & 1);
@@ -355,8 +392,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int t0 = start + j * kTile;
       const int live = min(nsub, (end - t0 + g - 1) / g);
       if (lane == 0) mbar_arrive_expect_tx(sh.bar(kBarKvFull + s), (uint32_t)(live * g) * kRowBytes);
+      TMLA_TRACE(0, j);
       __syncwarp();
-      if (pg >= 0) {
+      if (page_ok(j, lane, pg)) {
         const int t = t0 + lane * g;
         const int slot = p.block_table ? t % p.page_size : t;
         const uint32_t dst = sh.stage(s);
@@ -391,6 +429,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!waiter.wait(sh.bar(kBarKvFull + s), (j / kStages) & 1)) break;
         // Score buffer sb was last read for tile j-2.
         if (j >= 2 && !waiter.wait(sh.bar(kBarSEmpty0 + sb), ((j - 2) >> 1) & 1)) break;
+        TMLA_TRACE(1, j);
         tc_fence_after();
         const uint32_t st = sh.stage(s);
         const uint32_t d = tmem + kColS + 64 * sb;
@@ -425,6 +464,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < ntiles; ++j) {
         const int pb = j & 1;
         if (!waiter.wait(sh.bar(kBarPFull0 + pb), (j >> 1) & 1)) break;
+        TMLA_TRACE(2, j);
         tc_fence_after();
         const uint32_t st = sh.stage(j % kStages);
 #pragma unroll
@@ -440,20 +480,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       drain_wait(sh.bar(kBarDrainPV), 0);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ head-row warps (TMEM lane == head)
+  } else if (warp == kWarpRelay) {
+    // ------------------------------------------------------------ buffer-empty relay to the peer
+    // The local barriers are arrived with release semantics after the reads, so
+    // by the time this thread has acquired them every read of Sin / Pin has
+    // returned; only then may the peer overwrite those buffers.
+    if (lane == 0) {
+      const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty), peer);
+      const uint32_t poutempty_remote = map_to_rank(sh.bar(kBarPoutEmpty), peer);
+      for (int j = 0; j < ntiles; ++j) {
+        if (!waiter.wait(sh.bar(kBarSinRead), j & 1)) break;
+        mbar_arrive_cluster_relaxed(soutempty_remote);
+        if (!waiter.wait(sh.bar(kBarPinRead), j & 1)) break;
+        mbar_arrive_cluster_relaxed(poutempty_remote);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ head-row warps
+    // Warp w (4..15) works on TMEM lane quarter q = w % 4.  Within a quarter,
+    // lanes 32q + 16r + [0,16) are the heads this CTA owns, the other sixteen the
+    // peer's.  With the 16-lane shapes thread t holds head rows t/4 and t/4 + 8 of
+    // a 16-lane group (4 threads per row).
     const int quarter = warp & 3;
-    const int grp = (warp - 2) >> 2;  // 0: warps 2-5, 1: warps 6-9
-    const bool own = (uint32_t)(quarter >> 1) == rank;
-    const int row = quarter * 32 + lane;
-    const int idx = row & 63;  // index among the owner's 64 heads
-    const int h = h0 + row;
-    const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int role = warp >> 2;  // 1: softmax (own rows), 2: score sender, 3: P receiver (peer's rows)
+    const int L = lane >> 2, t4 = lane & 3;
+    const uint32_t q_lanes = (uint32_t)(quarter * 32) << 16;
+    const uint32_t own_lanes = (uint32_t)(quarter * 32 + 16 * (int)rank) << 16;
+    const uint32_t peer_lanes = (uint32_t)(quarter * 32 + 16 * (int)peer) << 16;
     const int last = ntiles - 1;
+    float* lstat = reinterpret_cast<float*>(smem_gen + kOffStat);  // [128 rows] (l, m)
 
-    if (grp == 0) {
-      // Q latent dims [0, 128) of this CTA's half -> TMEM (bf16 pairs; rows past H are zero).
-      const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b + (int64_t)h * p.q_stride_h +
+    if (role == 1) {
+      // Q latent dims [0, 128) of this CTA's half -> TMEM, all 32 rows of the quarter (rows past H are zero).
+      const int hq = h0 + quarter * 32 + lane;
+      const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
                       kHalfLatent * rank;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -461,34 +522,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           uint4 x = make_uint4(0, 0, 0, 0);
-          if (h < H) x = __ldg(reinterpret_cast<const uint4*>(qrow + 64 * c + 8 * v));
+          if (hq < H) x = __ldg(reinterpret_cast<const uint4*>(qrow + 64 * c + 8 * v));
           w[4 * v] = x.x;
           w[4 * v + 1] = x.y;
           w[4 * v + 2] = x.z;
           w[4 * v + 3] = x.w;
         }
-        tmem_st32(t_row + kColQ + 32 * c, w);
+        tmem_st32(tmem + q_lanes + kColQ + 32 * c, w);
       }
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sh.bar(kBarQFull));
-    }
 
-    if (own) {
-      // ---------------------------------------------------------- softmax, columns [32 grp, 32 grp + 32)
-      const int qi = quarter & 1;
-      const int t128 = qi * 64 + grp * 32 + lane;  // 0..127 over the four softmax warps
+      // ---------------------------------------------------------- softmax for my 16 rows of this quarter
       const float4* sin = reinterpret_cast<const float4*>(smem_gen + kOffSin);
-      float* maxbuf = reinterpret_cast<float*>(smem_gen + kOffMax);
       const uint32_t pin_remote = map_to_rank(sh.base + kOffPin, peer);
       const uint32_t alpha_remote = map_to_rank(sh.base + kOffAlpha, peer);
       const uint32_t fin_remote = map_to_rank(sh.base + kOffFin, peer);
       const uint32_t pinfull_remote = map_to_rank(sh.bar(kBarPinFull), peer);
       const uint32_t finfull_remote = map_to_rank(sh.bar(kBarFinFull), peer);
-      const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty), peer);
-      const bool arm = qi == 0 && grp == 0 && lane == 0;
-      float m_used = -INFINITY, l = 0.f;
+      const bool arm = quarter == 0 && lane == 0;
+      const int t128 = quarter * 32 + lane;
+      float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows L and L + 8 (partial sums)
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
@@ -497,11 +553,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        TMLA_TRACE_IF(quarter == 0, 3, j);
         tc_fence_after();
         float s[32];
         {
           uint32_t r[32];
-          tmem_ld32(t_row + kColS + 64 * sb + 32 * grp, r);
+          tmem_ld16x256_x8(tmem + own_lanes + kColS + 64 * sb, r);
           tc_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(r[i]);
@@ -513,65 +570,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        TMLA_TRACE_IF(quarter == 0, 4, j);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float4 v = sin[(8 * grp + c) * 64 + idx];
+          const float4 v = sin[(quarter * 8 + c) * 32 + lane];
           s[4 * c] += v.x;
           s[4 * c + 1] += v.y;
           s[4 * c + 2] += v.z;
           s[4 * c + 3] += v.w;
         }
+        // Sin has been read: a local release-arrive; warp 3 forwards it to the peer.
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster_relaxed(soutempty_remote);
+        if (lane == 0) mbar_arrive(sh.bar(kBarSinRead));
+        TMLA_TRACE_IF(quarter == 0, 5, j);
 
-        // Online softmax (base 2) with lazy rescaling; the row max is shared by the two halves.
-        const int nvalid = min(kTile, end - (start + j * kTile)) - 32 * grp;
-        float mx = -INFINITY;
+        // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
+        const int nvalid = min(kTile, end - (start + j * kTile));
+        float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          s[i] = (i < nvalid) ? s[i] * args.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[i]);
+          const int col = 8 * (i >> 2) + 2 * t4 + (i & 1);
+          s[i] = (col < nvalid) ? s[i] * args.scale_log2 : -INFINITY;
+          if (i & 2)
+            mx_b = fmaxf(mx_b, s[i]);
+          else
+            mx_a = fmaxf(mx_a, s[i]);
         }
-        maxbuf[((sb * 2 + qi) * 2 + grp) * 32 + lane] = mx;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sh.bar(kBarHalf0 + qi));
-        if (!waiter.wait(sh.bar(kBarHalf0 + qi), j & 1)) {
-          ok = false;
-          break;
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        float al_a = 1.f, al_b = 1.f;
+        const bool need_a = mx_a > m_a + kRescaleThreshold, need_b = mx_b > m_b + kRescaleThreshold;
+        if (need_a) {
+          al_a = ex2(m_a - mx_a);  // 0 on the first tile (m = -inf)
+          m_a = mx_a;
         }
-        mx = fmaxf(mx, maxbuf[((sb * 2 + qi) * 2 + (grp ^ 1)) * 32 + lane]);
-        float alpha = 1.f;
-        const bool need = mx > m_used + kRescaleThreshold;
-        if (need) {
-          alpha = ex2(m_used - mx);  // 0 on the first tile (m_used = -inf)
-          m_used = mx;
+        if (need_b) {
+          al_b = ex2(m_b - mx_b);
+          m_b = mx_b;
         }
-        uint32_t pk[16];
-        float sum = 0.f;
+        uint32_t pw[16];
+        float sum_a = 0.f, sum_b = 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float a = ex2(s[2 * i] - m_used), c2 = ex2(s[2 * i + 1] - m_used);
-          sum += a + c2;
-          pk[i] = pack2(a, c2, kFp16);
+        for (int k = 0; k < 8; ++k) {
+          const float p0 = ex2(s[4 * k] - m_a), p1 = ex2(s[4 * k + 1] - m_a);
+          const float p2 = ex2(s[4 * k + 2] - m_b), p3 = ex2(s[4 * k + 3] - m_b);
+          sum_a += p0 + p1;
+          sum_b += p2 + p3;
+          pw[2 * k] = pack2(p0, p1, kFp16);
+          pw[2 * k + 1] = pack2(p2, p3, kFp16);
         }
-        l = l * alpha + sum;  // this half's share of the row sum
-        // Ship P (and the rescale factor) to the peer's copy of these heads' rows.
+        l_a = l_a * al_a + sum_a;
+        l_b = l_b * al_b + sum_b;
+        TMLA_TRACE_IF(quarter == 0, 6, j);
+        // Ship P (and the rescale factors) to the peer's copy of these rows.
         if (j >= 1 && !waiter.wait(sh.bar(kBarPoutEmpty), (j - 1) & 1, true)) {
           ok = false;
           break;
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          st_async_u4(pin_remote + (uint32_t)((4 * grp + c) * 64 + idx) * 16u,
-                      make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]), pinfull_remote);
-        if (grp == 0) st_async_f1(alpha_remote + (uint32_t)idx * 4u, alpha, pinfull_remote);
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          st_async_u4(pin_remote + (uint32_t)((quarter * 4 + c) * 32 + lane) * 16u,
+                      make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]), pinfull_remote);
+        if (t4 == 0) st_async_f2(alpha_remote + (uint32_t)(quarter * 8 + L) * 8u, al_a, al_b, pinfull_remote);
+        TMLA_TRACE_IF(quarter == 0, 7, j);
+        if (j > 0 && __any_sync(0xffffffffu, need_a || need_b)) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          rescale_o(t_row, 128 * grp, 4, alpha);
+          rescale_rows16(tmem + own_lanes, al_a, al_b);
         }
         // P buffer sb was last read by PV(j-2).
         if (j >= 2 && !waiter.wait(sh.bar(kBarPvDone0 + sb), ((j - 2) >> 1) & 1)) {
@@ -579,43 +649,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        tmem_st16(t_row + kColP + 32 * sb + 16 * grp, pk);
+        tmem_st16x128_x8(tmem + own_lanes + kColP + 32 * sb, pw);
         tc_wait_st();
-        if (nvalid + 32 * grp < kTile)
-          zero_tail_rows(smem_gen + kOffStages + (j % kStages) * kStageBytes, nvalid + 32 * grp, t128);
+        if (nvalid < kTile) zero_tail_rows(smem_gen + kOffStages + (j % kStages) * kStageBytes, nvalid, t128);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarPFull0 + sb));
+        TMLA_TRACE_IF(quarter == 0, 8, j);
       }
-      // Row sum = both halves' shares; the peer normalises its half of these rows with it.
-      maxbuf[256 + (qi * 2 + grp) * 32 + lane] = l;
+      // Row sums: add the four threads' shares.
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+      const int row_a = quarter * 32 + 16 * (int)rank + L;
+      if (t4 == 0) {
+        st_async_f4(fin_remote + (uint32_t)(quarter * 8 + L) * 16u, l_a, m_a, l_b, m_b, finfull_remote);
+        lstat[2 * row_a] = l_a;
+        lstat[2 * (row_a + 8)] = l_b;
+        const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int hh = h0 + row_a + 8 * e;
+          const float l = e ? l_b : l_a, m = e ? m_b : m_a;
+          if (hh < H) {
+            const float lse2 = l > 0.f ? m + log2f(l) : -INFINITY;
+            if (final_out) {
+              if (p.lse) p.lse[(int64_t)b * p.lse_stride_b + hh] = l > 0.f ? lse2 * kLn2 : -INFINITY;
+            } else {
+              p.ws_lse[((int64_t)b * H + hh) * p.num_splits + split] = lse2;
+            }
+          }
+        }
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(sh.bar(kBarHalf0 + qi));
-      if (waiter.wait(sh.bar(kBarHalf0 + qi), ntiles & 1))
-        l += maxbuf[256 + (qi * 2 + (grp ^ 1)) * 32 + lane];
-      else
-        ok = false;
-      if (grp == 0) st_async_f2(fin_remote + (uint32_t)idx * 8u, l, m_used, finfull_remote);
+      if (lane == 0) mbar_arrive(sh.bar(kBarStats));
+      // Epilogue share: output columns [0, 128) of all 32 rows of this quarter.
       bool have_o = ok && ntiles > 0;
+      have_o = waiter.wait(sh.bar(kBarStats), 0) && have_o;
       if (have_o) {
         have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
         tc_fence_after();
       }
-      write_rows<T>(p, t_row, have_o, b, h, split, rank, l > 0.f ? 1.f / l : 0.f, 128 * grp, 4);
-      if (h < H && grp == 0) {
-        const float lse2 = l > 0.f ? m_used + log2f(l) : -INFINITY;
-        const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
-        if (final_out) {
-          if (p.lse) p.lse[(int64_t)b * p.lse_stride_b + h] = l > 0.f ? lse2 * kLn2 : -INFINITY;
-        } else {
-          p.ws_lse[((int64_t)b * H + h) * p.num_splits + split] = lse2;
-        }
-      }
-    } else if (grp == 0) {
-      // ---------------------------------------------------------- score sender for the peer's 64 heads
+      const float l = lstat[2 * (quarter * 32 + lane)];
+      write_rows<T>(p, tmem + q_lanes, have_o, b, h0 + quarter * 32 + lane, split, rank, l > 0.f ? 1.f / l : 0.f,
+                    0, 4);
+    } else if (role == 2) {
+      // ---------------------------------------------------------- score sender for the peer's 16 rows
       const uint32_t sin_remote = map_to_rank(sh.base + kOffSin, peer);
       const uint32_t sinfull_remote = map_to_rank(sh.bar(kBarSinFull), peer);
-      const float2* fin = reinterpret_cast<const float2*>(smem_gen + kOffFin);
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
@@ -623,10 +705,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        TMLA_TRACE_IF(quarter == 0, 9, j);
         tc_fence_after();
-        uint32_t r0[32], r1[32];
-        tmem_ld32(t_row + kColS + 64 * sb, r0);
-        tmem_ld32(t_row + kColS + 64 * sb + 32, r1);
+        uint32_t r[32];
+        tmem_ld16x256_x8(tmem + peer_lanes + kColS + 64 * sb, r);
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -637,32 +719,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          st_async_u4(sin_remote + (uint32_t)(c * 64 + idx) * 16u,
-                      make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]), sinfull_remote);
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          st_async_u4(sin_remote + (uint32_t)((8 + c) * 64 + idx) * 16u,
-                      make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]), sinfull_remote);
+          st_async_u4(sin_remote + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
+                      make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote);
+        TMLA_TRACE_IF(quarter == 0, 10, j);
       }
-      // Epilogue share: output columns [0, 128) of these rows, normalised with the owner's row sum.
-      float l = 0.f;
+      // Epilogue share: output columns [128, 256) of all 32 rows of this quarter.
       bool have_o = ok && ntiles > 0;
-      if (waiter.wait(sh.bar(kBarFinFull), 0, true))
-        l = fin[idx].x;
-      else
-        have_o = false;
+      have_o = waiter.wait(sh.bar(kBarStats), 0) && have_o;
       if (have_o) {
         have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
         tc_fence_after();
       }
-      write_rows<T>(p, t_row, have_o, b, h, split, rank, l > 0.f ? 1.f / l : 0.f, 0, 4);
+      const float l = lstat[2 * (quarter * 32 + lane)];
+      write_rows<T>(p, tmem + q_lanes, have_o, b, h0 + quarter * 32 + lane, split, rank, l > 0.f ? 1.f / l : 0.f,
+                    128, 4);
     } else {
-      // ---------------------------------------------------------- P receiver for the peer's 64 heads
+      // ---------------------------------------------------------- P receiver for the peer's 16 rows
       const uint4* pin = reinterpret_cast<const uint4*>(smem_gen + kOffPin);
-      const float* alpha_in = reinterpret_cast<const float*>(smem_gen + kOffAlpha);
-      const float2* fin = reinterpret_cast<const float2*>(smem_gen + kOffFin);
-      const uint32_t poutempty_remote = map_to_rank(sh.bar(kBarPoutEmpty), peer);
-      const bool arm = (quarter & 1) == 0 && lane == 0;
+      const float2* alpha_in = reinterpret_cast<const float2*>(smem_gen + kOffAlpha);
+      const float4* fin = reinterpret_cast<const float4*>(smem_gen + kOffFin);
+      const bool arm = quarter == 0 && lane == 0;
       if (arm) mbar_arrive_expect_tx(sh.bar(kBarFinFull), kFinBytes);
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
@@ -672,50 +748,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const float alpha = alpha_in[idx];
-        uint32_t pk[32];
+        TMLA_TRACE_IF(quarter == 0, 11, j);
+        const float2 al = alpha_in[quarter * 8 + L];
+        uint32_t pw[16];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = pin[c * 64 + idx];
-          pk[4 * c] = v.x;
-          pk[4 * c + 1] = v.y;
-          pk[4 * c + 2] = v.z;
-          pk[4 * c + 3] = v.w;
+        for (int c = 0; c < 4; ++c) {
+          const uint4 v = pin[(quarter * 4 + c) * 32 + lane];
+          pw[4 * c] = v.x;
+          pw[4 * c + 1] = v.y;
+          pw[4 * c + 2] = v.z;
+          pw[4 * c + 3] = v.w;
         }
+        // Pin has been read: a local release-arrive; warp 3 forwards it to the peer.
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster_relaxed(poutempty_remote);
-        const bool need = j > 0 && alpha != 1.f;
+        if (lane == 0) mbar_arrive(sh.bar(kBarPinRead));
+        const bool need = j > 0 && (al.x != 1.f || al.y != 1.f);
         if (__any_sync(0xffffffffu, need)) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          rescale_o(t_row, 0, 8, need ? alpha : 1.f);
+          rescale_rows16(tmem + peer_lanes, al.x, al.y);
         }
         if (j >= 2 && !waiter.wait(sh.bar(kBarPvDone0 + pb), ((j - 2) >> 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        tmem_st32(t_row + kColP + 32 * pb, pk);
+        tmem_st16x128_x8(tmem + peer_lanes + kColP + 32 * pb, pw);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarPFull0 + pb));
+        TMLA_TRACE_IF(quarter == 0, 12, j);
       }
-      // Epilogue share: output columns [128, 256) of these rows.
-      float l = 0.f;
-      bool have_o = ok && ntiles > 0;
-      if (waiter.wait(sh.bar(kBarFinFull), 0, true))
-        l = fin[idx].x;
-      else
-        have_o = false;
-      if (have_o) {
-        have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
-        tc_fence_after();
+      // The owner's final row sums for the epilogue.
+      if (waiter.wait(sh.bar(kBarFinFull), 0, true) && t4 == 0) {
+        const float4 f = fin[quarter * 8 + L];
+        const int row_a = quarter * 32 + 16 * (int)peer + L;
+        lstat[2 * row_a] = f.x;
+        lstat[2 * (row_a + 8)] = f.z;
       }
-      write_rows<T>(p, t_row, have_o, b, h, split, rank, l > 0.f ? 1.f / l : 0.f, 128, 4);
+      (void)ok;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sh.bar(kBarStats));
     }
   }
 
@@ -817,3 +894,9 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
 }
 
 }  // namespace tmla
+
+#ifdef TMLA_TRACE_ENABLED
+extern "C" int tmla_trace_copy(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, tmla::sm100::g_trace, sizeof(tmla::sm100::g_trace));
+}
+#endif
