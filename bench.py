@@ -59,6 +59,13 @@ def decode_bytes(total_tokens, batch, heads, elt=2):
     return float(total_tokens * D_QK + batch * heads * D_QK + batch * heads * D_V) * elt
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant kernel,
+# from the ncu capture summarised in profiles/ (re-captured whenever the kernel changes).
+NCU_TRAFFIC = {
+    ("cfg2", "sm100"): (160.0e6, "profiles/mla_sm100_split_kernel__cfg2_B32_S4096.md"),
+}
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -89,7 +96,7 @@ def make_workload(cfg, device, seed):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples every 200 ms while running."""
+    """nvidia-smi clock / throttle-reason samples every 50 ms while running."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -106,7 +113,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -135,7 +142,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "window": "soak of the same steps + timed region"}
 
 
 def cpu_oracle_rate(budget_s=10.0, seqlen=4096, heads=128):
@@ -203,6 +210,7 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "sm100", "generic"])
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (rank 0, N=1)")
+    ap.add_argument("--clock-soak", type=float, default=0.6, help="seconds of untimed steps under the clock sampler")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -241,13 +249,21 @@ def main(argv=None):
         step()
     torch.cuda.synchronize()
 
-    # ---- timed region: K steps, L2 flushed before each, events around each step.
+    # ---- timed region: K steps, L2 flushed before each, events around each step.  The clock
+    # sampler (nvidia-smi, 50 ms period) runs from a short soak of the same steps just before
+    # the timed region to its end: the timed region alone is only a few milliseconds long.
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < args.clock_soak:
+            for _ in range(8):
+                flush.zero_()
+                step()
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
@@ -343,7 +359,8 @@ def main(argv=None):
         "peak": hbm if bound == "hbm" else tflops_peak,
         "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
         "frac": (achieved_gbs / hbm) if bound == "hbm" else (achieved_tf / tflops_peak),
-        "traffic": None,
+        "traffic": NCU_TRAFFIC.get((args.config, kname), (None, None))[0],
+        "traffic_source": NCU_TRAFFIC.get((args.config, kname), (None, "not captured for this config"))[1],
         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
         "kernel": f"stage 1 ({kname})",
         "kernel_us": kern_ms * 1e3,
