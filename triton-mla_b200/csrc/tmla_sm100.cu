@@ -195,6 +195,19 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool fp16) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// `a` plus a term that is always 0 but is computed from `v` (min(~v, v) < 2^31)
+// by instructions the compiler cannot fold away.  A shared-memory operation at
+// the returned address cannot issue before the loads that produced `v` have
+// returned their data: the register scoreboard holds it until then.
+__device__ __forceinline__ uint32_t after_loads(uint32_t a, uint32_t v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .b32 n;\n\tnot.b32 n, %1;\n\tmin.u32 n, n, %1;\n\tshr.u32 n, n, 31;\n\tadd.u32 %0, %2, n;\n\t}"
+      : "=r"(r)
+      : "r"(v), "r"(a));
+  return r;
+}
+
 // O[r, :] *= alpha_r for the 16 TMEM lanes at `lanes` (256 fp32 columns, in place):
 // thread t scales lane t/4 by alpha_a and lane t/4 + 8 by alpha_b.
 __device__ __forceinline__ void rescale_rows16(uint32_t lanes, float alpha_a, float alpha_b) {
@@ -482,9 +495,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kWarpRelay) {
     // ------------------------------------------------------------ buffer-empty relay to the peer
-    // The local barriers are arrived with release semantics after the reads, so
-    // by the time this thread has acquired them every read of Sin / Pin has
-    // returned; only then may the peer overwrite those buffers.
+    // The readers arrive on the local barriers only once their loads of Sin / Pin
+    // have returned data (see after_loads), so when this thread sees a phase
+    // complete the peer may overwrite those buffers.
     if (lane == 0) {
       const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty), peer);
       const uint32_t poutempty_remote = map_to_rank(sh.bar(kBarPoutEmpty), peer);
@@ -571,17 +584,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         TMLA_TRACE_IF(quarter == 0, 4, j);
+        uint32_t dep = 0;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const float4 v = sin[(quarter * 8 + c) * 32 + lane];
+          dep ^= __float_as_uint(v.x) ^ __float_as_uint(v.y) ^ __float_as_uint(v.z) ^ __float_as_uint(v.w);
           s[4 * c] += v.x;
           s[4 * c + 1] += v.y;
           s[4 * c + 2] += v.z;
           s[4 * c + 3] += v.w;
         }
-        // Sin has been read: a local release-arrive; warp 3 forwards it to the peer.
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sh.bar(kBarSinRead));
+        // Sin has been read: a local arrive that warp 3 forwards to the peer, which may then
+        // overwrite Sin.  The arrive's address depends on every loaded word, so it cannot
+        // issue while a load of this warp is still in flight (a warp's loads complete for
+        // all lanes at once).
+        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead), dep));
         TMLA_TRACE_IF(quarter == 0, 5, j);
 
         // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
@@ -751,6 +768,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         TMLA_TRACE_IF(quarter == 0, 11, j);
         const float2 al = alpha_in[quarter * 8 + L];
         uint32_t pw[16];
+        uint32_t dep = __float_as_uint(al.x) ^ __float_as_uint(al.y);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint4 v = pin[(quarter * 4 + c) * 32 + lane];
@@ -758,10 +776,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           pw[4 * c + 1] = v.y;
           pw[4 * c + 2] = v.z;
           pw[4 * c + 3] = v.w;
+          dep ^= v.x ^ v.y ^ v.z ^ v.w;
         }
-        // Pin has been read: a local release-arrive; warp 3 forwards it to the peer.
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sh.bar(kBarPinRead));
+        // Pin has been read: a local arrive (address dependent on every loaded word, as for
+        // Sin) that warp 3 forwards to the peer.
+        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarPinRead), dep));
         const bool need = j > 0 && (al.x != 1.f || al.y != 1.f);
         if (__any_sync(0xffffffffu, need)) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
