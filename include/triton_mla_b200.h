@@ -101,6 +101,21 @@ typedef struct TmlaDecodeParams {
    Replaces `mla_decode` (kernel.py:204-323) after its host-side validation. */
 int tmla_decode(const TmlaDecodeParams* p, void* stream);
 
+/* Whole decode without any allocation.  No counterpart in the reference: it is
+   for callers that cannot allocate device memory (an FFI host without a device
+   allocator of its own, or a serving loop that must not call cudaMalloc, which
+   can synchronise the device).  Same as tmla_decode except that p->ws_o and
+   p->ws_lse are ignored: the split partials go to a fixed array of
+   TMLA_NOALLOC_SCRATCH_BYTES of device memory that the library holds on every
+   GPU that loads it, until exit.  A call needing more workspace than that
+   (tmla_workspace_bytes) returns TMLA_ERR_WORKSPACE; num_splits == 1 needs none.
+   The first call on a device looks up the array's device address (make it
+   before any stream capture).  All calls share the array: calls that can
+   overlap on the GPU (different streams or host threads) race on it; calls on
+   one stream are safe.  Allocates nothing (no cudaMalloc / cudaFree). */
+#define TMLA_NOALLOC_SCRATCH_BYTES (32u << 20)
+int tmla_decode_noalloc(const TmlaDecodeParams* p, void* stream);
+
 /* Stage 1 only: writes ws_o / ws_lse for every (request, head, split).
    Replaces the `_mla_decode_stage1` launch (kernel.py:276-302). */
 int tmla_decode_partial(const TmlaDecodeParams* p, void* stream);

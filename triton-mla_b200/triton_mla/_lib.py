@@ -37,9 +37,12 @@ KERNEL_SM100 = 2
 
 FLAG_PARTIAL_ONLY = 0x1
 
+NOALLOC_SCRATCH_BYTES = 32 << 20
+
 # Every symbol the header declares; tests check the library exports all of them.
 EXPORTED = (
     "tmla_decode",
+    "tmla_decode_noalloc",
     "tmla_decode_partial",
     "tmla_combine",
     "tmla_num_splits",
@@ -117,6 +120,8 @@ def load() -> ctypes.CDLL:
     i32, i64, vp, f32p = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p
     lib.tmla_decode.argtypes = [P, vp]
     lib.tmla_decode.restype = ctypes.c_int
+    lib.tmla_decode_noalloc.argtypes = [P, vp]
+    lib.tmla_decode_noalloc.restype = ctypes.c_int
     lib.tmla_decode_partial.argtypes = [P, vp]
     lib.tmla_decode_partial.restype = ctypes.c_int
     lib.tmla_combine.argtypes = [f32p, f32p, vp, i64, i64, f32p, i64, i32, i32, i32, i32, i32, vp]
