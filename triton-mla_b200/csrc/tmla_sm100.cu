@@ -11,38 +11,42 @@
 // needs O = 128 x 512 fp32 (all 512 TMEM columns of one SM) plus room for the
 // scores, so the two CTAs of a cluster split the latent dimension:
 //   CTA r holds latent dims [256r, 256r+256) and RoPE dims [512+32r, 544+32r)
-//   of Q and of every 64-token cache tile (4-stage TMA ring), and accumulates
-//   O[:, 256r:256r+256] for all 128 heads in TMEM.
+//   of Q and of every 64-token cache tile, and accumulates O[:, 256r:256r+256]
+//   for all 128 heads in TMEM.
 //   * QK: each CTA computes a partial S = Q_r . K_r^T (128 heads x 64 tokens,
 //     fp32) into one of two TMEM score buffers.
 //   * Softmax rows are split too.  Within each 32-lane TMEM quarter q the
 //     sixteen lanes 32q + 16r + [0,16) are the heads CTA r owns.  Each CTA
 //     sends the partial score rows of the heads it does not own to the peer
-//     (16 KB per tile over distributed shared memory); the owner adds them to
-//     its own partial, runs the online softmax and sends the 16-bit P rows
-//     (8 KB) and the rescale factors back, so both CTAs hold the same P for all
-//     128 heads in one of two TMEM P buffers.
-//   * PV: each CTA accumulates O_r += P . V_r with V_r the latent half of the
+//     (16 KB per tile over distributed shared memory, double-buffered); the
+//     owner adds them to its own partial and runs the online softmax.
+//   * P lives in shared memory, in the 128B-swizzled K-major layout the PV MMA
+//     reads as its A operand: the owner writes its 16 rows per quarter into its
+//     own P buffer and copies the same 2 KB (contiguous) into the peer's buffer
+//     with one bulk copy, together with the rows' rescale factors.
+//   * PV: each CTA accumulates O_r += P . V_r with V_r the latent part of the
 //     tile it already holds: the cache is read from HBM once and no MMA is
-//     duplicated.
-// Score and P buffers are double-buffered and QK and PV are issued by
-// different warps, so QK of tile j+1 and the score swap of tile j+1 run while
-// tile j is in the softmax.
+//     duplicated.  Both CTAs' PV commits are counted on a barrier in each CTA,
+//     so a P buffer is rewritten only after both CTAs have read it.
+// Cache tiles flow through two rings: the latent part (V as well as K) is held
+// until PV (4 stages), the RoPE part only until QK (2 slots).  Score and P
+// buffers are double-buffered and QK and PV are issued by different warps, so
+// QK of tile j+1 and the score swap of tile j+1 run while tile j is in the
+// softmax.
 //
-// TMEM (512 columns): O half 256 | Q latent dims [0,128) of the half 64 |
-// S0 64 | S1 64 | P0 32 | P1 32.  Q latent dims [128,256) of the half and the
-// RoPE half sit in shared memory (A operand of the remaining K steps).
+// TMEM (512 columns): O half 256 | Q latent half 128 | S0 64 | S1 64.  The Q
+// RoPE half sits in shared memory (A operand of the last two K steps).
 //
 // Warp roles (512 threads).  warp 0: TMA producer (block table -> page
 // coordinates); warp 1: TMEM allocation and QK issue; warp 2: PV issue;
-// warp 3: forwards "buffer read" signals to the peer.
+// warp 3: forwards "score buffer read" signals to the peer.
 // Warps 4-15 work on TMEM lane quarter w % 4 (the only lanes a warp can reach),
 // one warp of each role per quarter, so every SM sub-partition runs one
 // softmax warp:
 //   warps 4-7    softmax of the 16 owned rows (4 threads per row, 16-lane TMEM
-//                access shapes), P and rescale factors to the peer
+//                access shapes), P to both CTAs' P buffers, O rescale
 //   warps 8-11   score senders: ship the peer-owned partial rows to the owner
-//   warps 12-15  P receivers: write the owner's P rows into TMEM, rescale O
+//   warps 12-15  wait for the peer's P rows, rescale O for them
 // O is rescaled lazily: only when a row maximum grows by more than 2^8.  The
 // output is written by warps 4-11, one thread per row.
 //
@@ -64,7 +68,7 @@ namespace sm100 {
 __device__ unsigned long long g_trace[16 * 256];
 #define TMLA_TRACE_IF(cond, k, j)                                                                         \
   do {                                                                                                    \
-    if (tracing && (cond) && lane == 0 && (j) < 256) g_trace[(k) * 256 + (j)] = tmla::ptx::globaltimer(); \
+    if (tracing && (cond) && lane == 0 && (j) < 256) g_trace[(k) * 256 + (j)] = clock64();                 \
   } while (0)
 #else
 #define TMLA_TRACE_IF(cond, k, j) \
@@ -76,39 +80,45 @@ __device__ unsigned long long g_trace[16 * 256];
 using namespace ptx;
 
 constexpr int kTile = 64;                 // tokens per pipeline stage
-constexpr int kStages = 4;                // cache-tile ring depth
+constexpr int kStages = 4;                // latent cache-tile ring depth (held until PV)
+constexpr int kRopeSlots = 2;             // RoPE cache-tile ring depth (held until QK)
 constexpr int kThreads = 512;
 constexpr int kHalfLatent = 256;          // latent columns per CTA
 constexpr int kHalfRope = 32;             // RoPE columns per CTA
 constexpr uint32_t kBoxBytes = kTile * 128;                 // one 64-token x 64-dim swizzled box
 constexpr uint32_t kRopeBytes = kTile * kHalfRope * 2;      // 64 tokens x 32 dims
-constexpr uint32_t kStageBytes = 4 * kBoxBytes + kRopeBytes;  // 36864
+constexpr uint32_t kStageBytes = 4 * kBoxBytes;               // 32768: latent boxes of one tile
 constexpr uint32_t kRowBytes = (kHalfLatent + kHalfRope) * 2;  // cache bytes per token per CTA (576)
 constexpr uint32_t kQBoxBytes = 128 * 128;                  // 128 heads x 64 dims, swizzled
 constexpr uint32_t kQRopeBytes = 128 * kHalfRope * 2;       // 8192
 constexpr uint32_t kSinBytes = 64 * kTile * 4;              // 16384: peer's partial S for my 64 heads
-constexpr uint32_t kPinBytes = 64 * kTile * 2;              // 8192: owner's P for the peer's 64 heads
+constexpr uint32_t kPBufBytes = 128 * kTile * 2;            // 16384: P of all 128 rows, SW128 K-major
+constexpr uint32_t kPPeerBytes = 64 * kTile * 2;            // 8192: the rows of P that come from the peer
 constexpr uint32_t kAlphaBytes = 64 * 4;                    // rescale factors that come with P
 constexpr uint32_t kFinBytes = 64 * 8;                      // final (l, m) of the peer's heads
 constexpr uint32_t kStatBytes = 128 * 8;  // final (l, m) of all 128 rows for the epilogue
 
 constexpr uint32_t kOffStages = 0;
-constexpr uint32_t kOffQLat = kOffStages + kStages * kStageBytes;
-constexpr uint32_t kOffQRope = kOffQLat + 2 * kQBoxBytes;
+constexpr uint32_t kOffRope = kOffStages + kStages * kStageBytes;
+constexpr uint32_t kOffPBuf = kOffRope + kRopeSlots * kRopeBytes;  // P buffers: A operand of PV (1024-aligned)
+constexpr uint32_t kOffQRope = kOffPBuf + 2 * kPBufBytes;
 constexpr uint32_t kOffSin = kOffQRope + kQRopeBytes;
-constexpr uint32_t kOffPin = kOffSin + kSinBytes;
-constexpr uint32_t kOffAlpha = kOffPin + kPinBytes;
-constexpr uint32_t kOffFin = kOffAlpha + kAlphaBytes;
-constexpr uint32_t kOffStat = kOffFin + kFinBytes;
-constexpr uint32_t kOffBar = kOffStat + kStatBytes;
-constexpr uint32_t kNumBars = 2 * kStages + 19;
+constexpr uint32_t kOffAlpha = kOffSin + 2 * kSinBytes;    // Sin and alpha are double-buffered
+constexpr uint32_t kOffBar = kOffAlpha + 2 * kAlphaBytes;
+// The epilogue's row statistics and the peer's final (l, m) reuse the RoPE ring:
+// both are written only after the last QK of the CTA has completed.
+constexpr uint32_t kOffFin = kOffRope;
+constexpr uint32_t kOffStat = kOffRope + kFinBytes;
+static_assert(kFinBytes + kStatBytes <= kRopeSlots * kRopeBytes, "epilogue scratch must fit in the RoPE ring");
+static_assert(kOffPBuf % 1024 == 0, "P buffers must be 1024-byte aligned for the 128-byte swizzle");
+constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 26;
 constexpr uint32_t kOffMisc = kOffBar + ((kNumBars * 8 + 63) / 64) * 64;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory layout exceeds the 227 KB per-CTA limit");
 
 constexpr uint32_t kColO = 0;
-constexpr uint32_t kColQ = 256;
-constexpr uint32_t kColS = 320;   // + 64 * buffer
-constexpr uint32_t kColP = 448;   // + 32 * buffer
+constexpr uint32_t kColQ = 256;   // Q latent dims [0, 256) of the half: 128 columns
+constexpr uint32_t kColS = 384;   // + 64 * buffer
 
 constexpr int kWarpProducer = 0;
 constexpr int kWarpQK = 1;
@@ -122,7 +132,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 between
 enum : uint32_t {
   kBarKvFull = 0,
   kBarKvEmpty = kStages,
-  kBarQFull = 2 * kStages,
+  kBarRopeEmpty = 2 * kStages,      // QK of the tile in this RoPE slot has completed
+  kBarQFull = 2 * kStages + kRopeSlots,
   kBarSFull0,
   kBarSFull1,
   kBarSEmpty0,
@@ -131,22 +142,30 @@ enum : uint32_t {
   kBarPFull1,
   kBarPvDone0,
   kBarPvDone1,
-  kBarSinFull,     // peer's partial score rows landed in my Sin buffer
-  kBarSoutEmpty,   // peer has consumed what my score senders last sent
-  kBarPinFull,     // owner's P rows (+ rescale factors) landed in my Pin buffer
-  kBarPoutEmpty,   // peer has consumed the P rows my softmax warps last sent
+  kBarSinFull0,    // peer's partial score rows landed in my Sin buffer 0 / 1
+  kBarSinFull1,
+  kBarSoutEmpty0,  // peer has consumed what my score senders sent into its Sin buffer 0 / 1
+  kBarSoutEmpty1,
+  kBarPinFull0,    // the peer's P rows (+ rescale factors) landed in my P buffer 0 / 1
+  kBarPinFull1,
+  kBarPairPvDone0, // PV of the tile in P buffer 0 / 1 has completed in both CTAs (count 2)
+  kBarPairPvDone1,
   kBarFinFull,     // owner's final (l, m) of the peer's heads landed
   kBarDrainQK,
   kBarDrainPV,
   kBarStats,       // every row's final (l, m) is in shared memory for the epilogue
-  kBarSinRead,     // my softmax warps have read Sin (forwarded to the peer's SoutEmpty)
-  kBarPinRead,     // my P receivers have read Pin (forwarded to the peer's PoutEmpty)
+  kBarSinRead0,    // my softmax warps have read Sin buffer 0 / 1 (forwarded to the peer's SoutEmpty)
+  kBarSinRead1,
+  kBarCount,
 };
+
+static_assert(kBarCount <= kNumBars, "barrier area too small");
 
 struct Shared {
   uint32_t base;  // 1024-aligned shared address of the layout above
   __device__ uint32_t bar(uint32_t i) const { return base + kOffBar + 8 * i; }
   __device__ uint32_t stage(uint32_t s) const { return base + kOffStages + s * kStageBytes; }
+  __device__ uint32_t rope(uint32_t r) const { return base + kOffRope + r * kRopeBytes; }
 };
 
 // A wait that gives up after kWaitNs or as soon as another role gave up.
@@ -303,7 +322,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   Waiter waiter{abort_flag, p.status};
 #ifdef TMLA_TRACE_ENABLED
   const bool tracing = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-  if (tracing && threadIdx.x == 0) g_trace[15 * 256] = globaltimer();
+  if (tracing && threadIdx.x == 0) g_trace[15 * 256] = clock64();
 #endif
 
   if (threadIdx.x == 0) {
@@ -313,18 +332,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(sh.bar(kBarKvFull + s), 1);
       mbar_init(sh.bar(kBarKvEmpty + s), 1);
     }
+    for (int r = 0; r < kRopeSlots; ++r) mbar_init(sh.bar(kBarRopeEmpty + r), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(sh.bar(kBarSFull0 + i), 1);
       mbar_init(sh.bar(kBarSEmpty0 + i), 8);
       mbar_init(sh.bar(kBarPFull0 + i), 8);
       mbar_init(sh.bar(kBarPvDone0 + i), 1);
     }
-    mbar_init(sh.bar(kBarSinFull), 1);
-    mbar_init(sh.bar(kBarSoutEmpty), 1);
-    mbar_init(sh.bar(kBarPinFull), 1);
-    mbar_init(sh.bar(kBarPoutEmpty), 1);
-    mbar_init(sh.bar(kBarSinRead), 4);
-    mbar_init(sh.bar(kBarPinRead), 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(sh.bar(kBarSinFull0 + i), 1);
+      mbar_init(sh.bar(kBarSoutEmpty0 + i), 1);
+      mbar_init(sh.bar(kBarSinRead0 + i), 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(sh.bar(kBarPinFull0 + i), 1);
+      mbar_init(sh.bar(kBarPairPvDone0 + i), 2);
+    }
     mbar_init(sh.bar(kBarFinFull), 1);
     mbar_init(sh.bar(kBarDrainQK), 1);
     mbar_init(sh.bar(kBarDrainPV), 1);
@@ -365,10 +388,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint64_t pol_stream = policy_evict_first();
     if (lane == 0) {
       const uint64_t pol_q = policy_evict_last();
-      mbar_arrive_expect_tx(sh.bar(kBarQFull), 2 * kQBoxBytes + kQRopeBytes);
-      for (int k = 0; k < 2; ++k)
-        tma_load_3d(sh.base + kOffQLat + k * kQBoxBytes, &tm_q_lat, sh.bar(kBarQFull),
-                    kHalfLatent * rank + 128 + 64 * k, h0, b, pol_q);
+      mbar_arrive_expect_tx(sh.bar(kBarQFull), kQRopeBytes);
       tma_load_3d(sh.base + kOffQRope, &tm_q_rope, sh.bar(kBarQFull), 512 + kHalfRope * rank, h0, b, pol_q);
     }
     // Page id of sub-box `sb` of tile `j` (-1: past the end of the request).
@@ -397,9 +417,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int j = 0; j < ntiles; ++j) {
       int pg = pg_next;
       pg_next = page_of(j + 1, lane);
-      const int s = j % kStages;
+      const int s = j % kStages, rs = j % kRopeSlots;
       bool ok = true;
       if (lane == 0 && j >= kStages) ok = waiter.wait(sh.bar(kBarKvEmpty + s), ((j / kStages) - 1) & 1);
+      if (lane == 0 && ok && j >= kRopeSlots) ok = waiter.wait(sh.bar(kBarRopeEmpty + rs), ((j / kRopeSlots) - 1) & 1);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       const int t0 = start + j * kTile;
@@ -416,8 +437,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < 4; ++kb)
           tma_load_3d(dst + kb * kBoxBytes + lane * g * 128, &tm_kv_lat, bar, kHalfLatent * rank + 64 * kb, slot, pg,
                       pol_stream);
-        tma_load_3d(dst + 4 * kBoxBytes + lane * g * (kHalfRope * 2), &tm_kv_rope, bar, 512 + kHalfRope * rank, slot,
-                    pg, pol_stream);
+        tma_load_3d(sh.rope(rs) + lane * g * (kHalfRope * 2), &tm_kv_rope, bar, 512 + kHalfRope * rank, slot, pg,
+                    pol_stream);
       }
       issued = j + 1;
     }
@@ -435,7 +456,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t fmt = kFp16 ? 0u : 1u;
       const uint32_t idesc = idesc_f16(fmt, 128, kTile, 0);
-      const uint32_t q_lat = sh.base + kOffQLat, q_rope = sh.base + kOffQRope;
+      const uint32_t q_rope = sh.base + kOffQRope;
       bool ok = ntiles == 0 || waiter.wait(sh.bar(kBarQFull), 0);
       for (int j = 0; ok && j < ntiles; ++j) {
         const int s = j % kStages, sb = j & 1;
@@ -444,26 +465,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (j >= 2 && !waiter.wait(sh.bar(kBarSEmpty0 + sb), ((j - 2) >> 1) & 1)) break;
         TMLA_TRACE(1, j);
         tc_fence_after();
-        const uint32_t st = sh.stage(s);
+        const uint32_t st = sh.stage(s), rp = sh.rope(j % kRopeSlots);
         const uint32_t d = tmem + kColS + 64 * sb;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const uint64_t bdesc = smem_desc(st + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024, kSwizzle128B);
-          if (k < 8) {
-            mma_ts(d, tmem + kColQ + k * 8, bdesc, idesc, k > 0 ? 1u : 0u);
-          } else {
-            const uint64_t adesc = smem_desc(q_lat + ((k - 8) >> 2) * kQBoxBytes + (k & 3) * 32, 16, 1024,
-                                             kSwizzle128B);
-            mma_ss(d, adesc, bdesc, idesc, 1u);
-          }
+          mma_ts(d, tmem + kColQ + k * 8, bdesc, idesc, k > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const uint64_t adesc = smem_desc(q_rope + k * 32, 16, 512, kSwizzle64B);
-          const uint64_t bdesc = smem_desc(st + 4 * kBoxBytes + k * 32, 16, 512, kSwizzle64B);
+          const uint64_t bdesc = smem_desc(rp + k * 32, 16, 512, kSwizzle64B);
           mma_ss(d, adesc, bdesc, idesc, 1u);
         }
         mma_commit(sh.bar(kBarSFull0 + sb));
+        mma_commit(sh.bar(kBarRopeEmpty + j % kRopeSlots));
       }
       mma_commit(sh.bar(kBarDrainQK));
       drain_wait(sh.bar(kBarDrainQK), 0);
@@ -474,38 +490,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t fmt = kFp16 ? 0u : 1u;
       const uint32_t idesc = idesc_f16(fmt, 128, kHalfLatent, 1);
+      const uint32_t pairdone_remote = map_to_rank(sh.bar(kBarPairPvDone0), peer);  // + 8 * buffer
       for (int j = 0; j < ntiles; ++j) {
         const int pb = j & 1;
         if (!waiter.wait(sh.bar(kBarPFull0 + pb), (j >> 1) & 1)) break;
         TMLA_TRACE(2, j);
         tc_fence_after();
-        const uint32_t st = sh.stage(j % kStages);
+        const uint32_t st = sh.stage(j % kStages), pbuf = sh.base + kOffPBuf + pb * kPBufBytes;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
+          // A = P: 128 rows x 16 tokens, K-major 128B-swizzled (same layout as a Q box).
           // B = V: 16 tokens x 256 latent dims, MN-major 128B-swizzled, 64-dim boxes 8 KB apart.
+          const uint64_t adesc = smem_desc(pbuf + kk * 32, 16, 1024, kSwizzle128B);
           const uint64_t bdesc = smem_desc(st + kk * 16 * 128, kBoxBytes, 1024, kSwizzle128B);
-          mma_ts(tmem + kColO, tmem + kColP + 32 * pb + kk * 8, bdesc, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ss(tmem + kColO, adesc, bdesc, idesc, (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(sh.bar(kBarKvEmpty + j % kStages));
         mma_commit(sh.bar(kBarPvDone0 + pb));
+        // Both CTAs count this PV on their pair barrier: P buffer pb is free once both have run.
+        mma_commit(sh.bar(kBarPairPvDone0 + pb));
+        mma_commit_cluster(pairdone_remote + 8u * pb);
       }
       mma_commit(sh.bar(kBarDrainPV));
       drain_wait(sh.bar(kBarDrainPV), 0);
+      // The peer's commits on this CTA's pair barriers have all landed once their last
+      // phases completed; only then may this CTA exit.
+      for (int j = max(0, ntiles - 2); j < ntiles; ++j) drain_wait(sh.bar(kBarPairPvDone0 + (j & 1)), (j >> 1) & 1);
     }
     __syncwarp();
   } else if (warp == kWarpRelay) {
     // ------------------------------------------------------------ buffer-empty relay to the peer
-    // The readers arrive on the local barriers only once their loads of Sin / Pin
-    // have returned data (see after_loads), so when this thread sees a phase
-    // complete the peer may overwrite those buffers.
+    // The readers arrive on the local barriers only once their loads of Sin have
+    // returned data (see after_loads), so when this thread sees a phase complete
+    // the peer may overwrite that buffer.
     if (lane == 0) {
-      const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty), peer);
-      const uint32_t poutempty_remote = map_to_rank(sh.bar(kBarPoutEmpty), peer);
+      const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty0), peer);  // + 8 * buffer
       for (int j = 0; j < ntiles; ++j) {
-        if (!waiter.wait(sh.bar(kBarSinRead), j & 1)) break;
-        mbar_arrive_cluster_relaxed(soutempty_remote);
-        if (!waiter.wait(sh.bar(kBarPinRead), j & 1)) break;
-        mbar_arrive_cluster_relaxed(poutempty_remote);
+        if (!waiter.wait(sh.bar(kBarSinRead0 + (j & 1)), (j >> 1) & 1)) break;
+        mbar_arrive_cluster_relaxed(soutempty_remote + 8u * (j & 1));
       }
     }
     __syncwarp();
@@ -525,12 +547,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float* lstat = reinterpret_cast<float*>(smem_gen + kOffStat);  // [128 rows] (l, m)
 
     if (role == 1) {
-      // Q latent dims [0, 128) of this CTA's half -> TMEM, all 32 rows of the quarter (rows past H are zero).
+      // Q latent dims of this CTA's half -> TMEM, all 32 rows of the quarter (rows past H are zero).
       const int hq = h0 + quarter * 32 + lane;
       const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
                       kHalfLatent * rank;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t w[32];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
@@ -550,10 +572,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
       // ---------------------------------------------------------- softmax for my 16 rows of this quarter
       const float4* sin = reinterpret_cast<const float4*>(smem_gen + kOffSin);
-      const uint32_t pin_remote = map_to_rank(sh.base + kOffPin, peer);
       const uint32_t alpha_remote = map_to_rank(sh.base + kOffAlpha, peer);
       const uint32_t fin_remote = map_to_rank(sh.base + kOffFin, peer);
-      const uint32_t pinfull_remote = map_to_rank(sh.bar(kBarPinFull), peer);
+      const uint32_t pinfull_remote = map_to_rank(sh.bar(kBarPinFull0), peer);  // + 8 * buffer
       const uint32_t finfull_remote = map_to_rank(sh.bar(kBarFinFull), peer);
       const bool arm = quarter == 0 && lane == 0;
       const int t128 = quarter * 32 + lane;
@@ -561,7 +582,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
-        if (arm) mbar_arrive_expect_tx(sh.bar(kBarSinFull), kSinBytes);
+        if (arm) mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + sb), kSinBytes);
         if (!waiter.wait(sh.bar(kBarSFull0 + sb), (j >> 1) & 1)) {
           ok = false;
           break;
@@ -579,7 +600,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
-        if (!waiter.wait(sh.bar(kBarSinFull), j & 1, true)) {
+        if (!waiter.wait(sh.bar(kBarSinFull0 + sb), (j >> 1) & 1, true)) {
           ok = false;
           break;
         }
@@ -587,7 +608,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t dep = 0;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float4 v = sin[(quarter * 8 + c) * 32 + lane];
+          const float4 v = sin[sb * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
           dep ^= __float_as_uint(v.x) ^ __float_as_uint(v.y) ^ __float_as_uint(v.z) ^ __float_as_uint(v.w);
           s[4 * c] += v.x;
           s[4 * c + 1] += v.y;
@@ -598,7 +619,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // overwrite Sin.  The arrive's address depends on every loaded word, so it cannot
         // issue while a load of this warp is still in flight (a warp's loads complete for
         // all lanes at once).
-        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead), dep));
+        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + sb), dep));
         TMLA_TRACE_IF(quarter == 0, 5, j);
 
         // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
@@ -641,16 +662,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         l_a = l_a * al_a + sum_a;
         l_b = l_b * al_b + sum_b;
         TMLA_TRACE_IF(quarter == 0, 6, j);
-        // Ship P (and the rescale factors) to the peer's copy of these rows.
-        if (j >= 1 && !waiter.wait(sh.bar(kBarPoutEmpty), (j - 1) & 1, true)) {
+        // P buffer sb (in both CTAs) was last read by PV(j-2).
+        if (j >= 2 && !waiter.wait(sh.bar(kBarPairPvDone0 + sb), ((j - 2) >> 1) & 1)) {
           ok = false;
           break;
         }
+        {
+          // Own rows of P into this CTA's buffer, in the 128B-swizzled K-major layout PV
+          // reads (row r: 128 bytes at r * 128, 16-byte chunk c at (c ^ (r & 7)) * 16): word
+          // t4 of chunk k holds this thread's tokens 8k + 2 t4 and 8k + 2 t4 + 1.
+          unsigned char* pbuf = smem_gen + kOffPBuf + sb * kPBufBytes;
+          const int ra = quarter * 32 + 16 * (int)rank + L, rb = ra + 8;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          st_async_u4(pin_remote + (uint32_t)((quarter * 4 + c) * 32 + lane) * 16u,
-                      make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]), pinfull_remote);
-        if (t4 == 0) st_async_f2(alpha_remote + (uint32_t)(quarter * 8 + L) * 8u, al_a, al_b, pinfull_remote);
+          for (int k = 0; k < 8; ++k) {
+            *reinterpret_cast<uint32_t*>(pbuf + ra * 128 + ((k ^ (ra & 7)) << 4) + 4 * t4) = pw[2 * k];
+            *reinterpret_cast<uint32_t*>(pbuf + rb * 128 + ((k ^ (rb & 7)) << 4) + 4 * t4) = pw[2 * k + 1];
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          // The same 16 rows (2 KB, contiguous) into the peer's buffer, with the rescale factors.
+          if (lane == 0) {
+            const uint32_t off = kOffPBuf + sb * kPBufBytes + (uint32_t)(quarter * 32 + 16 * (int)rank) * 128u;
+            bulk_copy_to_cta(map_to_rank(sh.base + off, peer), sh.base + off, 2048u, pinfull_remote + 8u * sb);
+          }
+          if (t4 == 0)
+            st_async_f2(alpha_remote + (uint32_t)sb * kAlphaBytes + (uint32_t)(quarter * 8 + L) * 8u, al_a, al_b,
+                        pinfull_remote + 8u * sb);
+        }
         TMLA_TRACE_IF(quarter == 0, 7, j);
         if (j > 0 && __any_sync(0xffffffffu, need_a || need_b)) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
@@ -660,14 +698,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           rescale_rows16(tmem + own_lanes, al_a, al_b);
         }
-        // P buffer sb was last read by PV(j-2).
-        if (j >= 2 && !waiter.wait(sh.bar(kBarPvDone0 + sb), ((j - 2) >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_st16x128_x8(tmem + own_lanes + kColP + 32 * sb, pw);
-        tc_wait_st();
         if (nvalid < kTile) zero_tail_rows(smem_gen + kOffStages + (j % kStages) * kStageBytes, nvalid, t128);
         tc_fence_before();
         __syncwarp();
@@ -714,7 +744,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (role == 2) {
       // ---------------------------------------------------------- score sender for the peer's 16 rows
       const uint32_t sin_remote = map_to_rank(sh.base + kOffSin, peer);
-      const uint32_t sinfull_remote = map_to_rank(sh.bar(kBarSinFull), peer);
+      const uint32_t sinfull_remote = map_to_rank(sh.bar(kBarSinFull0), peer);  // + 8 * buffer
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
@@ -730,14 +760,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
-        if (j >= 1 && !waiter.wait(sh.bar(kBarSoutEmpty), (j - 1) & 1, true)) {
+        if (j >= 2 && !waiter.wait(sh.bar(kBarSoutEmpty0 + sb), ((j - 2) >> 1) & 1, true)) {
           ok = false;
           break;
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          st_async_u4(sin_remote + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
-                      make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote);
+          st_async_u4(sin_remote + (uint32_t)sb * kSinBytes + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
+                      make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote + 8u * sb);
         TMLA_TRACE_IF(quarter == 0, 10, j);
       }
       // Epilogue share: output columns [128, 256) of all 32 rows of this quarter.
@@ -751,8 +781,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       write_rows<T>(p, tmem + q_lanes, have_o, b, h0 + quarter * 32 + lane, split, rank, l > 0.f ? 1.f / l : 0.f,
                     128, 4);
     } else {
-      // ---------------------------------------------------------- P receiver for the peer's 16 rows
-      const uint4* pin = reinterpret_cast<const uint4*>(smem_gen + kOffPin);
+      // ---------------------------------------------------------- the peer's 16 rows of P
+      // The owner copies its P rows straight into this CTA's P buffer; here only their
+      // arrival is awaited and O is rescaled for those rows when the owner's maximum moved.
       const float2* alpha_in = reinterpret_cast<const float2*>(smem_gen + kOffAlpha);
       const float4* fin = reinterpret_cast<const float4*>(smem_gen + kOffFin);
       const bool arm = quarter == 0 && lane == 0;
@@ -760,27 +791,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int pb = j & 1;
-        if (arm) mbar_arrive_expect_tx(sh.bar(kBarPinFull), kPinBytes + kAlphaBytes);
-        if (!waiter.wait(sh.bar(kBarPinFull), j & 1, true)) {
+        if (arm) mbar_arrive_expect_tx(sh.bar(kBarPinFull0 + pb), kPPeerBytes + kAlphaBytes);
+        if (!waiter.wait(sh.bar(kBarPinFull0 + pb), (j >> 1) & 1, true)) {
           ok = false;
           break;
         }
         TMLA_TRACE_IF(quarter == 0, 11, j);
-        const float2 al = alpha_in[quarter * 8 + L];
-        uint32_t pw[16];
-        uint32_t dep = __float_as_uint(al.x) ^ __float_as_uint(al.y);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 v = pin[(quarter * 4 + c) * 32 + lane];
-          pw[4 * c] = v.x;
-          pw[4 * c + 1] = v.y;
-          pw[4 * c + 2] = v.z;
-          pw[4 * c + 3] = v.w;
-          dep ^= v.x ^ v.y ^ v.z ^ v.w;
-        }
-        // Pin has been read: a local arrive (address dependent on every loaded word, as for
-        // Sin) that warp 3 forwards to the peer.
-        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarPinRead), dep));
+        const float2 al = alpha_in[pb * 32 + quarter * 8 + L];
         const bool need = j > 0 && (al.x != 1.f || al.y != 1.f);
         if (__any_sync(0xffffffffu, need)) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
@@ -790,13 +807,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           rescale_rows16(tmem + peer_lanes, al.x, al.y);
         }
-        if (j >= 2 && !waiter.wait(sh.bar(kBarPvDone0 + pb), ((j - 2) >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_st16x128_x8(tmem + peer_lanes + kColP + 32 * pb, pw);
-        tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarPFull0 + pb));
