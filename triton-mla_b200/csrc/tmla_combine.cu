@@ -3,8 +3,9 @@
 // Replaces the reference's `_mla_decode_stage2` (src/triton_mla/kernel.py:141-181):
 // same arithmetic (base-2 weights against the split maximum, an all-empty row
 // gives out 0 and lse -inf, the final LSE is converted to natural log), but
-// one warp per (request, head) row with 16-byte loads of the fp32 partials
-// instead of one 4-warp program per row with a serial split loop.
+// warps over (request, head, 128-column group) with 16-byte loads of the fp32
+// partials, 8 splits in flight, instead of one 4-warp program per row with a
+// serial split loop.
 #include "tmla_common.cuh"
 
 namespace tmla {
@@ -43,11 +44,66 @@ __device__ __forceinline__ __half cvt1<__half>(float v) { return __float2half_rn
 template <>
 __device__ __forceinline__ float cvt1<float>(float v) { return v; }
 
+// Vector path (d_v a multiple of 128, at most 64 splits): one warp per (row, group of
+// 128 columns); lane l owns columns 4l..4l+3 of the group.  The split weights sit in
+// two registers per lane (splits l and l + 32) and are broadcast by shuffles, and the
+// loads of 8 splits are issued before their FMAs, so a row costs S/8 memory round
+// trips instead of S.
+template <typename T>
+__global__ void __launch_bounds__(kCombineWarps * 32)
+    mla_combine_vec_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
+                           int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S,
+                           int DV) {
+  const int lane = threadIdx.x & 31;
+  const int groups = DV / 128;
+  const int64_t wid = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
+  if (wid >= (int64_t)B * H * groups) return;
+  const int64_t row = wid / groups;
+  const int grp = (int)(wid - row * groups);
+  const int b = (int)(row / H), h = (int)(row - (int64_t)b * H);
+  const float* L = ws_lse + row * S;
+
+  const float l0 = lane < S ? L[lane] : -INFINITY, l1 = lane + 32 < S ? L[lane + 32] : -INFINITY;
+  float m = fmaxf(l0, l1);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (m == -INFINITY) m = 0.f;
+  const float w0 = exp2f(l0 - m), w1 = exp2f(l1 - m);  // 0 for -inf (empty splits, lanes past S)
+  float wsum = w0 + w1;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+
+  const float4* src = reinterpret_cast<const float4*>(ws_o + row * (int64_t)S * DV + grp * 128) + lane;
+  const int64_t sstride = DV / 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < S; s0 += 8) {
+    float4 v[8];
+    float w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int s = s0 + u;
+      w[u] = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
+      v[u] = (s < S) ? __ldg(src + s * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc.x = fmaf(w[u], v[u].x, acc.x);
+      acc.y = fmaf(w[u], v[u].y, acc.y);
+      acc.z = fmaf(w[u], v[u].z, acc.z);
+      acc.w = fmaf(w[u], v[u].w, acc.w);
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
+  T* dst = out + (int64_t)b * osb + (int64_t)h * osh + grp * 128 + 4 * lane;
+  store4<T>(dst, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+  if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+}
+
+// General path (any d_v, any split count): one warp per row, serial over splits.
 template <typename T>
 __global__ void __launch_bounds__(kCombineWarps * 32)
     mla_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
-                       int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S, int DV,
-                       int vec_ok) {
+                       int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S, int DV) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
   if (row >= (int64_t)B * H) return;
@@ -63,44 +119,12 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
   const float* O = ws_o + row * (int64_t)S * DV;
   T* dst = out + (int64_t)b * osb + (int64_t)h * osh;
   float wsum = 0.f;
-  if (vec_ok) {
-    // DV % 128 == 0: lane owns float4 columns 4*lane + 128*k.
-    const int nk = DV / 128;  // <= 8 for DV <= 1024
-    float4 acc[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < S; ++s) {
-      const float w = exp2f(L[s] - m);
-      wsum += w;
-      if (w == 0.f) continue;
-      const float4* src = reinterpret_cast<const float4*>(O + (int64_t)s * DV) + lane;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (k < nk) {
-          float4 v = __ldg(src + k * 32);
-          acc[k].x = fmaf(w, v.x, acc[k].x);
-          acc[k].y = fmaf(w, v.y, acc[k].y);
-          acc[k].z = fmaf(w, v.z, acc[k].z);
-          acc[k].w = fmaf(w, v.w, acc[k].w);
-        }
-      }
-    }
-    const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (k < nk) {
-        float4 v = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
-        store4<T>(dst + 4 * lane + 128 * k, v);
-      }
-    }
-  } else {
-    for (int s = 0; s < S; ++s) wsum += exp2f(L[s] - m);
-    const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
-    for (int d = lane; d < DV; d += 32) {
-      float a = 0.f;
-      for (int s = 0; s < S; ++s) a = fmaf(exp2f(L[s] - m), O[(int64_t)s * DV + d], a);
-      dst[d] = cvt1<T>(a * inv);
-    }
+  for (int s = 0; s < S; ++s) wsum += exp2f(L[s] - m);
+  const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
+  for (int d = lane; d < DV; d += 32) {
+    float a = 0.f;
+    for (int s = 0; s < S; ++s) a = fmaf(exp2f(L[s] - m), O[(int64_t)s * DV + d], a);
+    dst[d] = cvt1<T>(a * inv);
   }
   if (lse && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
 }
@@ -110,11 +134,18 @@ static int launch_combine_t(const float* ws_o, const float* ws_lse, void* out, i
                             int64_t lsb, int B, int H, int S, int DV, cudaStream_t stream) {
   const int64_t rows = (int64_t)B * H;
   if (rows == 0) return 0;
-  int vec_ok = (DV % 128 == 0) && (DV <= 1024) && (osb % 4 == 0) && (osh % 4 == 0) &&
-               (((uintptr_t)out) % (4 * sizeof(T)) == 0) && (((uintptr_t)ws_o) % 16 == 0);
-  const unsigned grid = (unsigned)((rows + kCombineWarps - 1) / kCombineWarps);
-  mla_combine_kernel<T><<<grid, kCombineWarps * 32, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), osb, osh, lse,
-                                                                 lsb, B, H, S, DV, vec_ok);
+  const bool vec_ok = (DV % 128 == 0) && (S <= 64) && (osb % 4 == 0) && (osh % 4 == 0) &&
+                      (((uintptr_t)out) % (4 * sizeof(T)) == 0) && (((uintptr_t)ws_o) % 16 == 0);
+  if (vec_ok) {
+    const int64_t warps = rows * (DV / 128);
+    const unsigned grid = (unsigned)((warps + kCombineWarps - 1) / kCombineWarps);
+    mla_combine_vec_kernel<T><<<grid, kCombineWarps * 32, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), osb, osh,
+                                                                       lse, lsb, B, H, S, DV);
+  } else {
+    const unsigned grid = (unsigned)((rows + kCombineWarps - 1) / kCombineWarps);
+    mla_combine_kernel<T><<<grid, kCombineWarps * 32, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), osb, osh,
+                                                                   lse, lsb, B, H, S, DV);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
 }

@@ -82,6 +82,7 @@ using namespace ptx;
 constexpr int kTile = 64;                 // tokens per pipeline stage
 constexpr int kStages = 4;                // latent cache-tile ring depth (held until PV)
 constexpr int kRopeSlots = 2;             // RoPE cache-tile ring depth (held until QK)
+constexpr int kSinBufs = 2;               // score-exchange buffers
 constexpr int kThreads = 512;
 constexpr int kHalfLatent = 256;          // latent columns per CTA
 constexpr int kHalfRope = 32;             // RoPE columns per CTA
@@ -103,7 +104,7 @@ constexpr uint32_t kOffRope = kOffStages + kStages * kStageBytes;
 constexpr uint32_t kOffPBuf = kOffRope + kRopeSlots * kRopeBytes;  // P buffers: A operand of PV (1024-aligned)
 constexpr uint32_t kOffQRope = kOffPBuf + 2 * kPBufBytes;
 constexpr uint32_t kOffSin = kOffQRope + kQRopeBytes;
-constexpr uint32_t kOffAlpha = kOffSin + 2 * kSinBytes;    // Sin and alpha are double-buffered
+constexpr uint32_t kOffAlpha = kOffSin + kSinBufs * kSinBytes;  // alpha is double-buffered
 constexpr uint32_t kOffBar = kOffAlpha + 2 * kAlphaBytes;
 // The epilogue's row statistics and the peer's final (l, m) reuse the RoPE ring:
 // both are written only after the last QK of the CTA has completed.
@@ -526,8 +527,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty0), peer);  // + 8 * buffer
       for (int j = 0; j < ntiles; ++j) {
-        if (!waiter.wait(sh.bar(kBarSinRead0 + (j & 1)), (j >> 1) & 1)) break;
-        mbar_arrive_cluster_relaxed(soutempty_remote + 8u * (j & 1));
+        const int ib = j % kSinBufs;
+        if (!waiter.wait(sh.bar(kBarSinRead0 + ib), (j / kSinBufs) & 1)) break;
+        mbar_arrive_cluster_relaxed(soutempty_remote + 8u * ib);
       }
     }
     __syncwarp();
@@ -582,7 +584,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
-        if (arm) mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + sb), kSinBytes);
+        const int ib = j % kSinBufs;
+        if (arm) mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + ib), kSinBytes);
         if (!waiter.wait(sh.bar(kBarSFull0 + sb), (j >> 1) & 1)) {
           ok = false;
           break;
@@ -600,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
-        if (!waiter.wait(sh.bar(kBarSinFull0 + sb), (j >> 1) & 1, true)) {
+        if (!waiter.wait(sh.bar(kBarSinFull0 + ib), (j / kSinBufs) & 1, true)) {
           ok = false;
           break;
         }
@@ -608,7 +611,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t dep = 0;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float4 v = sin[sb * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
+          const float4 v = sin[ib * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
           dep ^= __float_as_uint(v.x) ^ __float_as_uint(v.y) ^ __float_as_uint(v.z) ^ __float_as_uint(v.w);
           s[4 * c] += v.x;
           s[4 * c + 1] += v.y;
@@ -619,16 +622,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // overwrite Sin.  The arrive's address depends on every loaded word, so it cannot
         // issue while a load of this warp is still in flight (a warp's loads complete for
         // all lanes at once).
-        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + sb), dep));
+        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + ib), dep));
         TMLA_TRACE_IF(quarter == 0, 5, j);
 
         // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
+        // Maxima are taken on the unscaled scores (softmax_scale > 0) and the scale is
+        // folded into the exponent's FMA; only a partial last tile needs masking.
         const int nvalid = min(kTile, end - (start + j * kTile));
+        if (nvalid < kTile) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = 8 * (i >> 2) + 2 * t4 + (i & 1);
+            if (col >= nvalid) s[i] = -INFINITY;
+          }
+        }
         float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int col = 8 * (i >> 2) + 2 * t4 + (i & 1);
-          s[i] = (col < nvalid) ? s[i] * args.scale_log2 : -INFINITY;
           if (i & 2)
             mx_b = fmaxf(mx_b, s[i]);
           else
@@ -636,8 +646,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2)) * args.scale_log2;
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2)) * args.scale_log2;
         float al_a = 1.f, al_b = 1.f;
         const bool need_a = mx_a > m_a + kRescaleThreshold, need_b = mx_b > m_b + kRescaleThreshold;
         if (need_a) {
@@ -652,8 +662,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         float sum_a = 0.f, sum_b = 0.f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float p0 = ex2(s[4 * k] - m_a), p1 = ex2(s[4 * k + 1] - m_a);
-          const float p2 = ex2(s[4 * k + 2] - m_b), p3 = ex2(s[4 * k + 3] - m_b);
+          const float sc = args.scale_log2;
+          const float p0 = ex2(fmaf(s[4 * k], sc, -m_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -m_a));
+          const float p2 = ex2(fmaf(s[4 * k + 2], sc, -m_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -m_b));
           sum_a += p0 + p1;
           sum_b += p2 + p3;
           pw[2 * k] = pack2(p0, p1, kFp16);
@@ -760,14 +771,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
-        if (j >= 2 && !waiter.wait(sh.bar(kBarSoutEmpty0 + sb), ((j - 2) >> 1) & 1, true)) {
+        // Into the peer's score buffer it last read for tile j - kSinBufs.
+        const int ib = j % kSinBufs;
+        if (j >= kSinBufs && !waiter.wait(sh.bar(kBarSoutEmpty0 + ib), ((j - kSinBufs) / kSinBufs) & 1, true)) {
           ok = false;
           break;
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          st_async_u4(sin_remote + (uint32_t)sb * kSinBytes + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
-                      make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote + 8u * sb);
+          st_async_u4(sin_remote + (uint32_t)ib * kSinBytes + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
+                      make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote + 8u * ib);
         TMLA_TRACE_IF(quarter == 0, 10, j);
       }
       // Epilogue share: output columns [128, 256) of all 32 rows of this quarter.
