@@ -164,6 +164,28 @@ def test_strided_inputs(device):
         check(out, lse, ref_out, ref_lse, lens)
 
 
+@pytest.mark.parametrize("num_splits", [1, 3])
+def test_strided_out_view_and_partial_head_tile(device, num_splits):
+    """The tcgen05 kernel writes its output with tensor-tile stores: a padded ``out=`` view
+    receives exactly its own rows and columns (the padding around it is untouched), and the
+    rows past H in the last 128-head tile are not written."""
+    lens = [300, 0, 129]
+    case = recipes.paged_case(lens, 129, 64, seed=31)
+    c = to_dev(case, device)
+    big = torch.full((3, 136, 520), 7.0, dtype=torch.bfloat16, device=device)
+    view = big[:, 3:132, 8:]
+    assert selected_kernel(c["q"], c["kv"], c["block_table"], num_splits=num_splits) == "sm100"
+    out, lse = mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          num_splits=num_splits, return_lse=True, out=view)
+    assert out.data_ptr() == view.data_ptr()
+    ref_out, ref_lse = oracle_of(case)
+    check(out, lse, ref_out, ref_lse, lens)
+    pad = torch.ones(big.shape, dtype=torch.bool, device=device)
+    pad[:, 3:132, 8:] = False
+    assert bool((big[pad] == 7.0).all()), "the output store wrote outside the out= view"
+    assert read_status(device) == 0
+
+
 def test_empty_batch(device):
     q = torch.zeros(0, 128, 576, dtype=torch.bfloat16, device=device)
     kv = torch.zeros(4, 64, 576, dtype=torch.bfloat16, device=device)

@@ -7,6 +7,7 @@
 // partials, 8 splits in flight, instead of one 4-warp program per row with a
 // serial split loop.
 #include "tmla_common.cuh"
+#include "tmla_ptx.cuh"
 
 namespace tmla {
 
@@ -54,6 +55,8 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     mla_combine_vec_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
                            int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S,
                            int DV) {
+  // Launched as a programmatic dependent of the split kernel: wait for its partials.
+  ptx::griddep_wait();
   const int lane = threadIdx.x & 31;
   const int groups = DV / 128;
   const int64_t wid = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
@@ -62,6 +65,13 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
   const int grp = (int)(wid - row * groups);
   const int b = (int)(row / H), h = (int)(row - (int64_t)b * H);
   const float* L = ws_lse + row * S;
+  const float4* src = reinterpret_cast<const float4*>(ws_o + row * (int64_t)S * DV + grp * 128) + lane;
+  const int64_t sstride = DV / 4;
+  // The first 8 splits' partials are requested before the LSEs have come back: the two
+  // loads do not depend on each other.
+  float4 v[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) v[u] = (u < S) ? __ldg(src + u * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
 
   const float l0 = lane < S ? L[lane] : -INFINITY, l1 = lane + 32 < S ? L[lane + 32] : -INFINITY;
   float m = fmaxf(l0, l1);
@@ -73,17 +83,14 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
 
-  const float4* src = reinterpret_cast<const float4*>(ws_o + row * (int64_t)S * DV + grp * 128) + lane;
-  const int64_t sstride = DV / 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int s0 = 0; s0 < S; s0 += 8) {
-    float4 v[8];
     float w[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int s = s0 + u;
       w[u] = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
-      v[u] = (s < S) ? __ldg(src + s * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s0 > 0) v[u] = (s < S) ? __ldg(src + s * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -104,6 +111,7 @@ template <typename T>
 __global__ void __launch_bounds__(kCombineWarps * 32)
     mla_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
                        int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S, int DV) {
+  ptx::griddep_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
   if (row >= (int64_t)B * H) return;
@@ -136,17 +144,28 @@ static int launch_combine_t(const float* ws_o, const float* ws_lse, void* out, i
   if (rows == 0) return 0;
   const bool vec_ok = (DV % 128 == 0) && (S <= 64) && (osb % 4 == 0) && (osh % 4 == 0) &&
                       (((uintptr_t)out) % (4 * sizeof(T)) == 0) && (((uintptr_t)ws_o) % 16 == 0);
+  // Programmatic dependent launch: the merge's launch overlaps the end of the split
+  // kernel, and its CTAs wait for the split kernel's writes (griddep_wait) before reading.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(kCombineWarps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  T* o = static_cast<T*>(out);
+  cudaError_t e;
   if (vec_ok) {
     const int64_t warps = rows * (DV / 128);
-    const unsigned grid = (unsigned)((warps + kCombineWarps - 1) / kCombineWarps);
-    mla_combine_vec_kernel<T><<<grid, kCombineWarps * 32, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), osb, osh,
-                                                                       lse, lsb, B, H, S, DV);
+    cfg.gridDim = dim3((unsigned)((warps + kCombineWarps - 1) / kCombineWarps));
+    e = cudaLaunchKernelEx(&cfg, mla_combine_vec_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
   } else {
-    const unsigned grid = (unsigned)((rows + kCombineWarps - 1) / kCombineWarps);
-    mla_combine_kernel<T><<<grid, kCombineWarps * 32, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), osb, osh,
-                                                                   lse, lsb, B, H, S, DV);
+    cfg.gridDim = dim3((unsigned)((rows + kCombineWarps - 1) / kCombineWarps));
+    e = cudaLaunchKernelEx(&cfg, mla_combine_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
   }
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
 }
 

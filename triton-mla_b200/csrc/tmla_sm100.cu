@@ -77,12 +77,29 @@ __device__ unsigned long long g_trace[16 * 256];
 #endif
 #define TMLA_TRACE(k, j) TMLA_TRACE_IF(true, k, j)
 
+// Per-CTA %globaltimer stamps of the phases of the kernel (off unless built with
+// -DTMLA_SPAN_ENABLED), read back with tmla_span_copy().
+#ifdef TMLA_SPAN_ENABLED
+constexpr int kSpanCtas = 4096;
+__device__ unsigned long long g_span[kSpanCtas * 8];
+#define TMLA_SPAN(k)                                                                                     \
+  do {                                                                                                   \
+    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);                \
+    if (cta_ < kSpanCtas) g_span[cta_ * 8 + (k)] = globaltimer();                                        \
+  } while (0)
+#else
+#define TMLA_SPAN(k) \
+  do {               \
+  } while (0)
+#endif
+
 using namespace ptx;
 
 constexpr int kTile = 64;                 // tokens per pipeline stage
 constexpr int kStages = 4;                // latent cache-tile ring depth (held until PV)
 constexpr int kRopeSlots = 2;             // RoPE cache-tile ring depth (held until QK)
 constexpr int kSinBufs = 2;               // score-exchange buffers
+static_assert(kSinBufs == 2, "one score-exchange buffer per softmax warpgroup");
 constexpr int kThreads = 512;
 constexpr int kHalfLatent = 256;          // latent columns per CTA
 constexpr int kHalfRope = 32;             // RoPE columns per CTA
@@ -105,14 +122,17 @@ constexpr uint32_t kOffPBuf = kOffRope + kRopeSlots * kRopeBytes;  // P buffers:
 constexpr uint32_t kOffQRope = kOffPBuf + 2 * kPBufBytes;
 constexpr uint32_t kOffSin = kOffQRope + kQRopeBytes;
 constexpr uint32_t kOffAlpha = kOffSin + kSinBufs * kSinBytes;  // alpha is double-buffered
-constexpr uint32_t kOffBar = kOffAlpha + 2 * kAlphaBytes;
+constexpr uint32_t kOffMx = kOffAlpha + 2 * kAlphaBytes;      // running maxima handed between the warpgroups
+constexpr uint32_t kOffWst = kOffMx + 2 * 64 * 4;              // each warpgroup's final (l, m) of the owned rows
+constexpr uint32_t kOffBar = kOffWst + 2 * 64 * 8;
 // The epilogue's row statistics and the peer's final (l, m) reuse the RoPE ring:
 // both are written only after the last QK of the CTA has completed.
 constexpr uint32_t kOffFin = kOffRope;
 constexpr uint32_t kOffStat = kOffRope + kFinBytes;
 static_assert(kFinBytes + kStatBytes <= kRopeSlots * kRopeBytes, "epilogue scratch must fit in the RoPE ring");
 static_assert(kOffPBuf % 1024 == 0, "P buffers must be 1024-byte aligned for the 128-byte swizzle");
-constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 26;
+static_assert(kStages * kStageBytes >= 8 * 128 * 128, "the epilogue tiles (128 KB) reuse the cache-tile ring");
+constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 36;
 constexpr uint32_t kOffMisc = kOffBar + ((kNumBars * 8 + 63) / 64) * 64;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory layout exceeds the 227 KB per-CTA limit");
@@ -157,6 +177,10 @@ enum : uint32_t {
   kBarStats,       // every row's final (l, m) is in shared memory for the epilogue
   kBarSinRead0,    // my softmax warps have read Sin buffer 0 / 1 (forwarded to the peer's SoutEmpty)
   kBarSinRead1,
+  kBarMaxA0,       // softmax warpgroup A (even tiles) published its running maximum, per quarter
+  kBarMaxB0 = kBarMaxA0 + 4,  // warpgroup B (odd tiles), per quarter
+  kBarWgStats = kBarMaxB0 + 4,  // both warpgroups' final (l, m) are in shared memory
+  kBarEpi,         // the epilogue tiles are staged (8 warps)
   kBarCount,
 };
 
@@ -255,44 +279,47 @@ __device__ __forceinline__ void zero_tail_rows(unsigned char* stage, int nvalid,
   fence_proxy_async_smem();
 }
 
-// Write columns [c0, c0 + 32*nchunks) of this CTA's output half for one head row.
+// Epilogue tiles: 128 rows x 128 bytes, 128B-swizzled (16-byte chunk k of row r at
+// (k ^ (r & 7)) * 16), one per TMA store box: 32 fp32 columns of the split partial, or
+// 64 16-bit columns of the final output.  They reuse the cache-tile ring, which is idle
+// once the last PV has completed.
+constexpr uint32_t kOutBoxBytes = 128 * 128;
+
+// Stage columns [32 c0, 32 (c0 + nchunks)) of this CTA's output half of row r (scaled by
+// inv; zeros when there is no output) into the epilogue tiles at `tiles`.
 template <typename T>
-__device__ __forceinline__ void write_rows(const TmlaDecodeParams& p, uint32_t t_row, bool have_o, int b, int h,
-                                           int split, uint32_t rank, float inv, int c0, int nchunks) {
+__device__ __forceinline__ void stage_rows(unsigned char* tiles, uint32_t t_row, bool have_o, int r, float inv,
+                                           int c0, int nchunks, bool final_out) {
   constexpr bool kFp16 = std::is_same<T, __half>::value;
-  const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
-  const int H = p.num_heads;
 #pragma unroll 1
-  for (int c = 0; c < nchunks; ++c) {
+  for (int c = c0; c < c0 + nchunks; ++c) {
     uint32_t o[32];
     if (have_o) {
-      tmem_ld32(t_row + kColO + c0 + 32 * c, o);
+      tmem_ld32(t_row + kColO + 32 * c, o);
       tc_wait_ld();
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = 0u;
     }
-    if (h < H) {
-      const int col = kHalfLatent * rank + c0 + 32 * c;
-      if (final_out) {
-        T* dst = static_cast<T*>(p.out) + (int64_t)b * p.out_stride_b + (int64_t)h * p.out_stride_h + col;
+    if (final_out) {
+      unsigned char* row = tiles + (c >> 1) * kOutBoxBytes + r * 128;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint4 w;
-          w.x = pack2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv, kFp16);
-          w.y = pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv, kFp16);
-          w.z = pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv, kFp16);
-          w.w = pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv, kFp16);
-          *reinterpret_cast<uint4*>(dst + 8 * v) = w;
-        }
-      } else {
-        float* dst = p.ws_o + (((int64_t)b * H + h) * p.num_splits + split) * 512 + col;
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          *reinterpret_cast<float4*>(dst + 4 * v) =
-              make_float4(__uint_as_float(o[4 * v]) * inv, __uint_as_float(o[4 * v + 1]) * inv,
-                          __uint_as_float(o[4 * v + 2]) * inv, __uint_as_float(o[4 * v + 3]) * inv);
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = pack2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv, kFp16);
+        w.y = pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv, kFp16);
+        w.z = pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv, kFp16);
+        w.w = pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv, kFp16);
+        const int k = (c & 1) * 4 + v;
+        *reinterpret_cast<uint4*>(row + ((k ^ (r & 7)) << 4)) = w;
       }
+    } else {
+      unsigned char* row = tiles + c * kOutBoxBytes + r * 128;
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        *reinterpret_cast<float4*>(row + ((v ^ (r & 7)) << 4)) =
+            make_float4(__uint_as_float(o[4 * v]) * inv, __uint_as_float(o[4 * v + 1]) * inv,
+                        __uint_as_float(o[4 * v + 2]) * inv, __uint_as_float(o[4 * v + 3]) * inv);
     }
   }
 }
@@ -300,7 +327,7 @@ __device__ __forceinline__ void write_rows(const TmlaDecodeParams& p, uint32_t t
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_sm100_split_kernel(const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
-                           const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constant__ CUtensorMap tm_q_rope,
+                           const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_q_rope,
                            const __grid_constant__ KernelArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const TmlaDecodeParams& p = args.p;
@@ -326,6 +353,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (tracing && threadIdx.x == 0) g_trace[15 * 256] = clock64();
 #endif
 
+  if (threadIdx.x == 0) TMLA_SPAN(0);
+  // The request length, the block-table entries of the split and this CTA's Q rows are
+  // requested before the set-up below, so that their latency overlaps it.
+  const int len_in = __ldg(p.seqlens + b);
+  if (warp == kWarpProducer && p.block_table) {
+    // 32 lines of the block-table row around where this split starts when the request
+    // fills the table (a split of a shorter request starts earlier in the row).
+    const int cap_tiles = (p.bt_width * p.page_size + kTile - 1) / kTile;
+    const int per = (cap_tiles + p.num_splits - 1) / p.num_splits;
+    const int64_t first = (int64_t)split * per * kTile / p.page_size;  // entry index
+    const int64_t line = max((int64_t)0, first / 32 - 8) + lane;
+    if (line * 32 < p.bt_width) prefetch_l2(p.block_table + (int64_t)b * p.bt_stride + line * 32);
+  }
+  if (warp >= 4 && warp < 8) {
+    const int hq = h0 + (warp - 4) * 32 + lane;
+    if (hq < H) {
+      const char* qrow = reinterpret_cast<const char*>(static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b +
+                                                       (int64_t)hq * p.q_stride_h + kHalfLatent * rank);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) prefetch_l2(qrow + 128 * c);
+    }
+  }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     mbar_init(sh.bar(kBarQFull), 1 + 4);
@@ -337,7 +386,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(sh.bar(kBarSFull0 + i), 1);
       mbar_init(sh.bar(kBarSEmpty0 + i), 8);
-      mbar_init(sh.bar(kBarPFull0 + i), 8);
+      mbar_init(sh.bar(kBarPFull0 + i), 4);
       mbar_init(sh.bar(kBarPvDone0 + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -353,6 +402,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(sh.bar(kBarDrainQK), 1);
     mbar_init(sh.bar(kBarDrainPV), 1);
     mbar_init(sh.bar(kBarStats), 8);
+    mbar_init(sh.bar(kBarWgStats), 8);
+    mbar_init(sh.bar(kBarEpi), 8);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(sh.bar(kBarMaxA0 + q), 1);
+      mbar_init(sh.bar(kBarMaxB0 + q), 1);
+    }
     fence_mbar_init();
   }
   if (warp == kWarpQK) {
@@ -362,7 +417,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == kWarpProducer && lane == 0) {
     prefetch_tmap(&tm_kv_lat);
     prefetch_tmap(&tm_kv_rope);
-    prefetch_tmap(&tm_q_lat);
+    prefetch_tmap(&tm_out);
     prefetch_tmap(&tm_q_rope);
   }
   tc_fence_before();
@@ -370,9 +425,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // the peer's barriers are initialised before any remote arrive / st.async
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) TMLA_SPAN(1);
 
   // Token range of this split (whole 64-token tiles; see split_range).
-  int len = p.seqlens[b];
+  int len = len_in;
   const int cap = p.block_table ? p.bt_width * p.page_size : p.page_size;
   if (len < 0 || len > cap) {
     if (p.status && threadIdx.x == 0) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
@@ -428,6 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int live = min(nsub, (end - t0 + g - 1) / g);
       if (lane == 0) mbar_arrive_expect_tx(sh.bar(kBarKvFull + s), (uint32_t)(live * g) * kRowBytes);
       TMLA_TRACE(0, j);
+      if (lane == 0 && j == 0) TMLA_SPAN(2);
       __syncwarp();
       if (page_ok(j, lane, pg)) {
         const int t = t0 + lane * g;
@@ -465,6 +522,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // Score buffer sb was last read for tile j-2.
         if (j >= 2 && !waiter.wait(sh.bar(kBarSEmpty0 + sb), ((j - 2) >> 1) & 1)) break;
         TMLA_TRACE(1, j);
+        if (j == 0) TMLA_SPAN(3);
         tc_fence_after();
         const uint32_t st = sh.stage(s), rp = sh.rope(j % kRopeSlots);
         const uint32_t d = tmem + kColS + 64 * sb;
@@ -496,6 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int pb = j & 1;
         if (!waiter.wait(sh.bar(kBarPFull0 + pb), (j >> 1) & 1)) break;
         TMLA_TRACE(2, j);
+        if (j == ntiles - 1) TMLA_SPAN(4);
         tc_fence_after();
         const uint32_t st = sh.stage(j % kStages), pbuf = sh.base + kOffPBuf + pb * kPBufBytes;
 #pragma unroll
@@ -540,7 +599,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // peer's.  With the 16-lane shapes thread t holds head rows t/4 and t/4 + 8 of
     // a 16-lane group (4 threads per row).
     const int quarter = warp & 3;
-    const int role = warp >> 2;  // 1: softmax (own rows), 2: score sender, 3: P receiver (peer's rows)
+    const int role = warp >> 2;  // 1, 2: softmax warpgroups A (even tiles) and B (odd tiles); 3: score sender
     const int L = lane >> 2, t4 = lane & 3;
     const uint32_t q_lanes = (uint32_t)(quarter * 32) << 16;
     const uint32_t own_lanes = (uint32_t)(quarter * 32 + 16 * (int)rank) << 16;
@@ -548,45 +607,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int last = ntiles - 1;
     float* lstat = reinterpret_cast<float*>(smem_gen + kOffStat);  // [128 rows] (l, m)
 
-    if (role == 1) {
-      // Q latent dims of this CTA's half -> TMEM, all 32 rows of the quarter (rows past H are zero).
-      const int hq = h0 + quarter * 32 + lane;
-      const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
-                      kHalfLatent * rank;
+    if (role <= 2) {
+      const int wg = role - 1;  // this warpgroup runs the tiles j with j % 2 == wg
+      if (wg == 0) {
+        // Q latent dims of this CTA's half -> TMEM, all 32 rows of the quarter (rows past H are zero).
+        const int hq = h0 + quarter * 32 + lane;
+        const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
+                        kHalfLatent * rank;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t w[32];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[32];
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          uint4 x = make_uint4(0, 0, 0, 0);
-          if (hq < H) x = __ldg(reinterpret_cast<const uint4*>(qrow + 64 * c + 8 * v));
-          w[4 * v] = x.x;
-          w[4 * v + 1] = x.y;
-          w[4 * v + 2] = x.z;
-          w[4 * v + 3] = x.w;
+          for (int v = 0; v < 8; ++v) {
+            uint4 x = make_uint4(0, 0, 0, 0);
+            if (hq < H) x = __ldg(reinterpret_cast<const uint4*>(qrow + 64 * c + 8 * v));
+            w[4 * v] = x.x;
+            w[4 * v + 1] = x.y;
+            w[4 * v + 2] = x.z;
+            w[4 * v + 3] = x.w;
+          }
+          tmem_st32(tmem + q_lanes + kColQ + 32 * c, w);
         }
-        tmem_st32(tmem + q_lanes + kColQ + 32 * c, w);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sh.bar(kBarQFull));
       }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sh.bar(kBarQFull));
 
-      // ---------------------------------------------------------- softmax for my 16 rows of this quarter
+      // ---------------------------------------------------------- softmax of my 16 rows of this quarter
+      // Tiles alternate between the two warpgroups.  The running maximum of tile j-1
+      // comes from the other warpgroup through shared memory (one barrier per quarter);
+      // each warpgroup keeps partial row sums relative to the maximum of its own last tile.
+      // After its own rows, the warpgroup also takes the peer's P rows of the tile
+      // (copied straight into this CTA's P buffer) and rescales O for them when asked.
       const float4* sin = reinterpret_cast<const float4*>(smem_gen + kOffSin);
+      const float2* alpha_in = reinterpret_cast<const float2*>(smem_gen + kOffAlpha);
+      float* m_mine = reinterpret_cast<float*>(smem_gen + kOffMx) + 64 * wg;
+      const float* m_other = reinterpret_cast<const float*>(smem_gen + kOffMx) + 64 * (wg ^ 1);
       const uint32_t alpha_remote = map_to_rank(sh.base + kOffAlpha, peer);
-      const uint32_t fin_remote = map_to_rank(sh.base + kOffFin, peer);
       const uint32_t pinfull_remote = map_to_rank(sh.bar(kBarPinFull0), peer);  // + 8 * buffer
-      const uint32_t finfull_remote = map_to_rank(sh.bar(kBarFinFull), peer);
+      const uint32_t max_out = sh.bar((wg ? kBarMaxB0 : kBarMaxA0) + quarter);
+      const uint32_t max_in = sh.bar((wg ? kBarMaxA0 : kBarMaxB0) + quarter);
       const bool arm = quarter == 0 && lane == 0;
       const int t128 = quarter * 32 + lane;
+      const int orow = quarter * 16 + L;  // index of row L among this CTA's 64 owned rows (row L + 8: orow + 8)
+      if (wg == 1 && arm) mbar_arrive_expect_tx(sh.bar(kBarFinFull), kFinBytes);
       float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows L and L + 8 (partial sums)
       bool ok = true;
-      for (int j = 0; j < ntiles; ++j) {
-        const int sb = j & 1;
-        const int ib = j % kSinBufs;
-        if (arm) mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + ib), kSinBytes);
-        if (!waiter.wait(sh.bar(kBarSFull0 + sb), (j >> 1) & 1)) {
+      for (int j = wg; j < ntiles; j += 2) {
+        const int sb = wg;  // S, Sin, P and alpha buffer of this tile (j % 2)
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (arm) {
+          mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + sb), kSinBytes);
+          mbar_arrive_expect_tx(sh.bar(kBarPinFull0 + sb), kPPeerBytes + kAlphaBytes);
+        }
+        if (!waiter.wait(sh.bar(kBarSFull0 + sb), ph)) {
           ok = false;
           break;
         }
@@ -603,7 +678,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
-        if (!waiter.wait(sh.bar(kBarSinFull0 + ib), (j / kSinBufs) & 1, true)) {
+        if (!waiter.wait(sh.bar(kBarSinFull0 + sb), ph, true)) {
           ok = false;
           break;
         }
@@ -611,7 +686,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t dep = 0;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float4 v = sin[ib * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
+          const float4 v = sin[sb * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
           dep ^= __float_as_uint(v.x) ^ __float_as_uint(v.y) ^ __float_as_uint(v.z) ^ __float_as_uint(v.w);
           s[4 * c] += v.x;
           s[4 * c + 1] += v.y;
@@ -622,7 +697,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // overwrite Sin.  The arrive's address depends on every loaded word, so it cannot
         // issue while a load of this warp is still in flight (a warp's loads complete for
         // all lanes at once).
-        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + ib), dep));
+        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + sb), dep));
         TMLA_TRACE_IF(quarter == 0, 5, j);
 
         // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
@@ -648,33 +723,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2)) * args.scale_log2;
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2)) * args.scale_log2;
-        float al_a = 1.f, al_b = 1.f;
-        const bool need_a = mx_a > m_a + kRescaleThreshold, need_b = mx_b > m_b + kRescaleThreshold;
+        // The running maximum after tile j-1, published by the other warpgroup.
+        float mp_a = -INFINITY, mp_b = -INFINITY;
+        if (j > 0) {
+          if (!waiter.wait(max_in, (uint32_t)((j - 1) >> 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          mp_a = m_other[orow];
+          mp_b = m_other[orow + 8];
+        }
+        float mn_a = mp_a, mn_b = mp_b, al_a = 1.f, al_b = 1.f;
+        const bool need_a = mx_a > mp_a + kRescaleThreshold, need_b = mx_b > mp_b + kRescaleThreshold;
         if (need_a) {
-          al_a = ex2(m_a - mx_a);  // 0 on the first tile (m = -inf)
-          m_a = mx_a;
+          al_a = ex2(mp_a - mx_a);  // 0 on the first tile (m = -inf)
+          mn_a = mx_a;
         }
         if (need_b) {
-          al_b = ex2(m_b - mx_b);
-          m_b = mx_b;
+          al_b = ex2(mp_b - mx_b);
+          mn_b = mx_b;
         }
+        if (t4 == 0) {
+          m_mine[orow] = mn_a;
+          m_mine[orow + 8] = mn_b;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(max_out);
+        // This warpgroup's partial sums were relative to the maximum of its previous tile.
+        l_a = m_a == -INFINITY ? 0.f : l_a * ex2(m_a - mn_a);
+        l_b = m_b == -INFINITY ? 0.f : l_b * ex2(m_b - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
         uint32_t pw[16];
         float sum_a = 0.f, sum_b = 0.f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float sc = args.scale_log2;
-          const float p0 = ex2(fmaf(s[4 * k], sc, -m_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -m_a));
-          const float p2 = ex2(fmaf(s[4 * k + 2], sc, -m_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -m_b));
+          const float p0 = ex2(fmaf(s[4 * k], sc, -mn_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -mn_a));
+          const float p2 = ex2(fmaf(s[4 * k + 2], sc, -mn_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -mn_b));
           sum_a += p0 + p1;
           sum_b += p2 + p3;
           pw[2 * k] = pack2(p0, p1, kFp16);
           pw[2 * k + 1] = pack2(p2, p3, kFp16);
         }
-        l_a = l_a * al_a + sum_a;
-        l_b = l_b * al_b + sum_b;
+        l_a += sum_a;
+        l_b += sum_b;
         TMLA_TRACE_IF(quarter == 0, 6, j);
         // P buffer sb (in both CTAs) was last read by PV(j-2).
-        if (j >= 2 && !waiter.wait(sh.bar(kBarPairPvDone0 + sb), ((j - 2) >> 1) & 1)) {
+        if (j >= 2 && !waiter.wait(sh.bar(kBarPairPvDone0 + sb), (uint32_t)((j - 2) >> 1) & 1u)) {
           ok = false;
           break;
         }
@@ -702,7 +798,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         TMLA_TRACE_IF(quarter == 0, 7, j);
         if (j > 0 && __any_sync(0xffffffffu, need_a || need_b)) {
-          if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
+          if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), (uint32_t)((j - 1) >> 1) & 1u)) {
             ok = false;
             break;
           }
@@ -710,28 +806,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           rescale_rows16(tmem + own_lanes, al_a, al_b);
         }
         if (nvalid < kTile) zero_tail_rows(smem_gen + kOffStages + (j % kStages) * kStageBytes, nvalid, t128);
+        TMLA_TRACE_IF(quarter == 0, 8, j);
+        // The peer's rows of P(j) and their rescale factors.
+        if (!waiter.wait(sh.bar(kBarPinFull0 + sb), ph, true)) {
+          ok = false;
+          break;
+        }
+        TMLA_TRACE_IF(quarter == 0, 11, j);
+        const float2 al = alpha_in[sb * 32 + quarter * 8 + L];
+        if (__any_sync(0xffffffffu, j > 0 && (al.x != 1.f || al.y != 1.f))) {
+          if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), (uint32_t)((j - 1) >> 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          rescale_rows16(tmem + peer_lanes, al.x, al.y);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarPFull0 + sb));
-        TMLA_TRACE_IF(quarter == 0, 8, j);
+        TMLA_TRACE_IF(quarter == 0, 12, j);
       }
-      // Row sums: add the four threads' shares.
+      // Row sums: add the four threads' shares; both warpgroups' (l, m) meet in shared memory.
       l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
       l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
       l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
       l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-      const int row_a = quarter * 32 + 16 * (int)rank + L;
+      float2* wst = reinterpret_cast<float2*>(smem_gen + kOffWst);  // [2 warpgroups][64 owned rows]
       if (t4 == 0) {
-        st_async_f4(fin_remote + (uint32_t)(quarter * 8 + L) * 16u, l_a, m_a, l_b, m_b, finfull_remote);
-        lstat[2 * row_a] = l_a;
-        lstat[2 * (row_a + 8)] = l_b;
-        const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int hh = h0 + row_a + 8 * e;
-          const float l = e ? l_b : l_a, m = e ? m_b : m_a;
+        wst[64 * wg + orow] = make_float2(l_a, m_a);
+        wst[64 * wg + orow + 8] = make_float2(l_b, m_b);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sh.bar(kBarWgStats));
+      const bool stats_ok = waiter.wait(sh.bar(kBarWgStats), 0);
+      if (wg == 0) {
+        // Owned rows: the final maximum is the larger of the two warpgroups' last ones
+        // (maxima only grow); (l, m) go to the peer for its half of these rows' output.
+        if (lane < 16 && stats_ok) {
+          const int o = quarter * 16 + lane;
+          const float2 A = wst[o], Bw = wst[64 + o];
+          const float mf = fmaxf(A.y, Bw.y);
+          float l = 0.f;
+          if (A.y != -INFINITY) l += A.x * ex2(A.y - mf);
+          if (Bw.y != -INFINITY) l += Bw.x * ex2(Bw.y - mf);
+          const int row = quarter * 32 + 16 * (int)rank + lane;
+          st_async_f2(map_to_rank(sh.base + kOffFin, peer) + (uint32_t)o * 8u, l, mf,
+                      map_to_rank(sh.bar(kBarFinFull), peer));
+          lstat[2 * row] = l;
+          const int hh = h0 + row;
           if (hh < H) {
-            const float lse2 = l > 0.f ? m + log2f(l) : -INFINITY;
+            const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
+            const float lse2 = l > 0.f ? mf + log2f(l) : -INFINITY;
             if (final_out) {
               if (p.lse) p.lse[(int64_t)b * p.lse_stride_b + hh] = l > 0.f ? lse2 * kLn2 : -INFINITY;
             } else {
@@ -739,30 +865,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else {
+        // The peer's final row sums of its rows, for this CTA's half of their output.
+        const float2* fin = reinterpret_cast<const float2*>(smem_gen + kOffFin);
+        if (waiter.wait(sh.bar(kBarFinFull), 0, true) && lane < 16) {
+          const float2 f = fin[quarter * 16 + lane];
+          lstat[2 * (quarter * 32 + 16 * (int)peer + lane)] = f.x;
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(sh.bar(kBarStats));
-      // Epilogue share: output columns [0, 128) of all 32 rows of this quarter.
-      bool have_o = ok && ntiles > 0;
+      // Epilogue share: output columns [128 wg, 128 wg + 128) of all 32 rows of this quarter.
+      bool have_o = ok && stats_ok && ntiles > 0;
       have_o = waiter.wait(sh.bar(kBarStats), 0) && have_o;
       if (have_o) {
         have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
         tc_fence_after();
       }
+      if (wg == 0 && quarter == 0 && lane == 0) TMLA_SPAN(5);
       const float l = lstat[2 * (quarter * 32 + lane)];
-      write_rows<T>(p, tmem + q_lanes, have_o, b, h0 + quarter * 32 + lane, split, rank, l > 0.f ? 1.f / l : 0.f,
-                    0, 4);
-    } else if (role == 2) {
+      const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
+      stage_rows<T>(smem_gen + kOffStages, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
+                    4 * wg, 4, final_out);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sh.bar(kBarEpi));
+      if (wg == 0 && quarter == 0 && lane == 0) {
+        // One thread stores the staged half-tile; rows past H fall outside the tensor map
+        // and are not written.
+        if (waiter.wait(sh.bar(kBarEpi), 0)) {
+          if (final_out) {
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c)
+              tma_store_3d(&tm_out, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 64 * c, h0, b);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c)
+              tma_store_4d(&tm_out, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 32 * c, split,
+                           h0, b);
+          }
+          bulk_commit_group();
+          bulk_wait_group0();
+        }
+        TMLA_SPAN(6);
+      }
+    } else {
       // ---------------------------------------------------------- score sender for the peer's 16 rows
       const uint32_t sin_remote = map_to_rank(sh.base + kOffSin, peer);
       const uint32_t sinfull_remote = map_to_rank(sh.bar(kBarSinFull0), peer);  // + 8 * buffer
-      bool ok = true;
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
-        if (!waiter.wait(sh.bar(kBarSFull0 + sb), (j >> 1) & 1)) {
-          ok = false;
-          break;
-        }
+        if (!waiter.wait(sh.bar(kBarSFull0 + sb), (j >> 1) & 1)) break;
         TMLA_TRACE_IF(quarter == 0, 9, j);
         tc_fence_after();
         uint32_t r[32];
@@ -773,71 +926,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
         // Into the peer's score buffer it last read for tile j - kSinBufs.
         const int ib = j % kSinBufs;
-        if (j >= kSinBufs && !waiter.wait(sh.bar(kBarSoutEmpty0 + ib), ((j - kSinBufs) / kSinBufs) & 1, true)) {
-          ok = false;
-          break;
-        }
+        if (j >= kSinBufs && !waiter.wait(sh.bar(kBarSoutEmpty0 + ib), ((j - kSinBufs) / kSinBufs) & 1, true)) break;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           st_async_u4(sin_remote + (uint32_t)ib * kSinBytes + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
                       make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote + 8u * ib);
         TMLA_TRACE_IF(quarter == 0, 10, j);
       }
-      // Epilogue share: output columns [128, 256) of all 32 rows of this quarter.
-      bool have_o = ok && ntiles > 0;
-      have_o = waiter.wait(sh.bar(kBarStats), 0) && have_o;
-      if (have_o) {
-        have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
-        tc_fence_after();
-      }
-      const float l = lstat[2 * (quarter * 32 + lane)];
-      write_rows<T>(p, tmem + q_lanes, have_o, b, h0 + quarter * 32 + lane, split, rank, l > 0.f ? 1.f / l : 0.f,
-                    128, 4);
-    } else {
-      // ---------------------------------------------------------- the peer's 16 rows of P
-      // The owner copies its P rows straight into this CTA's P buffer; here only their
-      // arrival is awaited and O is rescaled for those rows when the owner's maximum moved.
-      const float2* alpha_in = reinterpret_cast<const float2*>(smem_gen + kOffAlpha);
-      const float4* fin = reinterpret_cast<const float4*>(smem_gen + kOffFin);
-      const bool arm = quarter == 0 && lane == 0;
-      if (arm) mbar_arrive_expect_tx(sh.bar(kBarFinFull), kFinBytes);
-      bool ok = true;
-      for (int j = 0; j < ntiles; ++j) {
-        const int pb = j & 1;
-        if (arm) mbar_arrive_expect_tx(sh.bar(kBarPinFull0 + pb), kPPeerBytes + kAlphaBytes);
-        if (!waiter.wait(sh.bar(kBarPinFull0 + pb), (j >> 1) & 1, true)) {
-          ok = false;
-          break;
-        }
-        TMLA_TRACE_IF(quarter == 0, 11, j);
-        const float2 al = alpha_in[pb * 32 + quarter * 8 + L];
-        const bool need = j > 0 && (al.x != 1.f || al.y != 1.f);
-        if (__any_sync(0xffffffffu, need)) {
-          if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), ((j - 1) >> 1) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          rescale_rows16(tmem + peer_lanes, al.x, al.y);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sh.bar(kBarPFull0 + pb));
-        TMLA_TRACE_IF(quarter == 0, 12, j);
-      }
-      // The owner's final row sums for the epilogue.
-      if (waiter.wait(sh.bar(kBarFinFull), 0, true) && t4 == 0) {
-        const float4 f = fin[quarter * 8 + L];
-        const int row_a = quarter * 32 + 16 * (int)peer + L;
-        lstat[2 * row_a] = f.x;
-        lstat[2 * (row_a + 8)] = f.z;
-      }
-      (void)ok;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sh.bar(kBarStats));
     }
   }
 
+  // The split merge, when it follows in the stream, may be scheduled once every CTA got here.
+  griddep_launch_dependents();
   // Teardown: both CTAs are done with each other's shared memory before either exits.
   tc_fence_before();
   __syncthreads();
@@ -846,6 +946,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) TMLA_SPAN(7);
 }
 
 // ---------------------------------------------------------------------------- host side
@@ -876,6 +977,20 @@ static int encode3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, 
   return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
 }
 
+// The fp32 split partials ws_o [batch, heads, splits, 512] as a 4-D map with boxes of
+// 32 columns x 1 split x 128 heads x 1 request.
+static int encode_partials(CUtensorMap* map, float* ws_o, int batch, int heads, int splits) {
+  auto fn = encode_fn();
+  if (!fn) return TMLA_ERR_CUDA;
+  cuuint64_t dims[4] = {512, (cuuint64_t)splits, (cuuint64_t)heads, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {512 * 4, (cuuint64_t)splits * 512 * 4, (cuuint64_t)heads * splits * 512 * 4};
+  cuuint32_t box[4] = {32, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws_o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
+}
+
 static int pow2_rows(int page) {
   int g = 64;
   while (g > 1 && page % g) g >>= 1;
@@ -902,7 +1017,7 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
       p.dtype == TMLA_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int g = p.block_table ? pow2_rows(p.page_size) : kTile;
   const uint64_t pages = p.block_table ? (uint64_t)p.num_pages : (uint64_t)p.batch;
-  CUtensorMap tm_lat, tm_rope, tm_q, tm_qlat;
+  CUtensorMap tm_lat, tm_rope, tm_q, tm_out;
   int rc = encode3d(&tm_lat, dt, p.kv, 576, (uint64_t)p.page_size, pages, (uint64_t)p.kv_stride_tok * 2,
                     (uint64_t)p.kv_stride_page * 2, 64, (uint32_t)g, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc)
@@ -911,9 +1026,11 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
   if (!rc)
     rc = encode3d(&tm_q, dt, p.q, 576, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.q_stride_h * 2,
                   (uint64_t)p.q_stride_b * 2, kHalfRope, 128, CU_TENSOR_MAP_SWIZZLE_64B);
-  if (!rc)
-    rc = encode3d(&tm_qlat, dt, p.q, 576, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.q_stride_h * 2,
-                  (uint64_t)p.q_stride_b * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
+  if (!rc && final_out)
+    rc = encode3d(&tm_out, dt, p.out, 512, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.out_stride_h * 2,
+                  (uint64_t)p.out_stride_b * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc && !final_out) rc = encode_partials(&tm_out, p.ws_o, p.batch, p.num_heads, p.num_splits);
   if (rc) return rc;
   KernelArgs a;
   a.p = p;
@@ -924,12 +1041,12 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
   if (p.dtype == TMLA_DTYPE_FP16) {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      mla_sm100_split_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_qlat, tm_q, a);
+      mla_sm100_split_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_q, a);
   } else {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
     if (e == cudaSuccess)
-      mla_sm100_split_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_qlat, tm_q, a);
+      mla_sm100_split_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_q, a);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
@@ -937,6 +1054,11 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
 
 }  // namespace tmla
 
+#ifdef TMLA_SPAN_ENABLED
+extern "C" int tmla_span_copy(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, tmla::sm100::g_span, sizeof(tmla::sm100::g_span));
+}
+#endif
 #ifdef TMLA_TRACE_ENABLED
 extern "C" int tmla_trace_copy(void* dst) {
   return (int)cudaMemcpyFromSymbol(dst, tmla::sm100::g_trace, sizeof(tmla::sm100::g_trace));
