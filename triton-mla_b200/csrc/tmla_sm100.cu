@@ -357,6 +357,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // The request length, the block-table entries of the split and this CTA's Q rows are
   // requested before the set-up below, so that their latency overlaps it.
   const int len_in = __ldg(p.seqlens + b);
+  const int cap = p.block_table ? p.bt_width * p.page_size : p.page_size;
+  const int g = args.rows_per_load;  // token rows per TMA box
+  const int nsub = kTile / g;
+  // The producer reads the page ids of its first tile as if the request filled its table:
+  // the first tile of a split then does not wait for the length and the table one after
+  // the other (when the guess is wrong they are read again once the length is known).
+  int spec_start = 0, pg_spec = 0;
+  if (warp == kWarpProducer) {
+    int spec_end;
+    split_range(cap, p.num_splits, split, spec_start, spec_end);
+    const int t = spec_start + lane * g;
+    if (lane < nsub && t < spec_end) pg_spec = p.block_table ? __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size) : b;
+  }
   if (warp == kWarpProducer && p.block_table) {
     // 32 lines of the block-table row around where this split starts when the request
     // fills the table (a split of a shorter request starts earlier in the row).
@@ -420,16 +433,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_out);
     prefetch_tmap(&tm_q_rope);
   }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // the peer's barriers are initialised before any remote arrive / st.async
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) TMLA_SPAN(1);
 
   // Token range of this split (whole 64-token tiles; see split_range).
   int len = len_in;
-  const int cap = p.block_table ? p.bt_width * p.page_size : p.page_size;
   if (len < 0 || len > cap) {
     if (p.status && threadIdx.x == 0) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
     len = len < 0 ? 0 : cap;
@@ -438,41 +444,77 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   split_range(len, p.num_splits, split, start, end);
   const int ntiles = end > start ? (end - start + kTile - 1) / kTile : 0;
 
-  if (warp == kWarpProducer) {
-    // ------------------------------------------------------------ TMA producer
-    const int g = args.rows_per_load;
-    const int nsub = kTile / g;
-    const uint64_t pol_stream = policy_evict_first();
-    if (lane == 0) {
-      const uint64_t pol_q = policy_evict_last();
-      mbar_arrive_expect_tx(sh.bar(kBarQFull), kQRopeBytes);
-      tma_load_3d(sh.base + kOffQRope, &tm_q_rope, sh.bar(kBarQFull), 512 + kHalfRope * rank, h0, b, pol_q);
+  // ------------------------------------------------------------ TMA producer, part 1
+  // The producer's barriers were initialised by its own lane 0 above, so Q's RoPE half
+  // and the first cache tile are requested before the CTA-wide and cluster-wide syncs.
+  const uint64_t pol_stream = policy_evict_first();
+  // Raw page id of sub-box `sb` of tile `j` (0 when the sub-box is past the end of
+  // the split); read ahead of use, checked by `page_ok` when used.
+  auto page_of = [&](int j, int sb) -> int {
+    const int t = start + j * kTile + sb * g;
+    if (sb >= nsub || t >= end || j >= ntiles) return 0;
+    if (!p.block_table) return b;
+    return __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size);
+  };
+  // Whether sub-box `sb` of tile `j` is inside the split; a page id outside the
+  // pool is reported and replaced by page 0 (its tokens are not trusted).
+  auto page_ok = [&](int j, int sb, int& pg) -> bool {
+    const int t = start + j * kTile + sb * g;
+    if (sb >= nsub || t >= end || j >= ntiles) return false;
+    if (pg < 0 || (int64_t)pg >= (int64_t)(p.block_table ? p.num_pages : p.batch)) {
+      if (p.status) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
+      pg = 0;
     }
-    // Page id of sub-box `sb` of tile `j` (-1: past the end of the request).
-    // Raw page id of sub-box `sb` of tile `j` (0 when the sub-box is past the end of
-    // the split); read ahead of use, checked by `page_ok` when used.
-    auto page_of = [&](int j, int sb) -> int {
-      const int t = start + j * kTile + sb * g;
-      if (sb >= nsub || t >= end || j >= ntiles) return 0;
-      if (!p.block_table) return b;
-      return __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size);
-    };
-    // Whether sub-box `sb` of tile `j` is inside the split; a page id outside the
-    // pool is reported and replaced by page 0 (its tokens are not trusted).
-    auto page_ok = [&](int j, int sb, int& pg) -> bool {
-      const int t = start + j * kTile + sb * g;
-      if (sb >= nsub || t >= end || j >= ntiles) return false;
-      if (pg < 0 || (int64_t)pg >= (int64_t)(p.block_table ? p.num_pages : p.batch)) {
-        if (p.status) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
-        pg = 0;
-      }
-      return true;
-    };
-    // Page ids are read one iteration before they are needed .
-    int pg_next = ntiles > 0 ? page_of(0, lane) : -1;
-    int issued = 0;
-    for (int j = 0; j < ntiles; ++j) {
-      int pg = pg_next;
+    return true;
+  };
+  // Loads of tile j (ring stage j % kStages, RoPE slot j % kRopeSlots) once both are free.
+  auto issue_tile = [&](int j, int pg) {
+    const int s = j % kStages, rs = j % kRopeSlots;
+    const int t0 = start + j * kTile;
+    const int live = min(nsub, (end - t0 + g - 1) / g);
+    if (lane == 0) mbar_arrive_expect_tx(sh.bar(kBarKvFull + s), (uint32_t)(live * g) * kRowBytes);
+    TMLA_TRACE(0, j);
+    if (lane == 0 && j == 0) TMLA_SPAN(2);
+    __syncwarp();
+    if (page_ok(j, lane, pg)) {
+      const int t = t0 + lane * g;
+      const int slot = p.block_table ? t % p.page_size : t;
+      const uint32_t dst = sh.stage(s);
+      const uint32_t bar = sh.bar(kBarKvFull + s);
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb)
+        tma_load_3d(dst + kb * kBoxBytes + lane * g * 128, &tm_kv_lat, bar, kHalfLatent * rank + 64 * kb, slot, pg,
+                    pol_stream);
+      tma_load_3d(sh.rope(rs) + lane * g * (kHalfRope * 2), &tm_kv_rope, bar, 512 + kHalfRope * rank, slot, pg,
+                  pol_stream);
+    }
+  };
+  int pg_next = -1;
+  if (warp == kWarpProducer) {
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(sh.bar(kBarQFull), kQRopeBytes);
+      tma_load_3d(sh.base + kOffQRope, &tm_q_rope, sh.bar(kBarQFull), 512 + kHalfRope * rank, h0, b,
+                  policy_evict_last());
+    }
+    if (ntiles > 0) {
+      issue_tile(0, start == spec_start ? pg_spec : page_of(0, lane));
+      pg_next = page_of(1, lane);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote arrive / st.async
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) TMLA_SPAN(1);
+
+  if (warp == kWarpProducer) {
+    // ------------------------------------------------------------ TMA producer, part 2
+    int issued = ntiles > 0 ? 1 : 0;
+    for (int j = 1; j < ntiles; ++j) {
+      const int pg = pg_next;
       pg_next = page_of(j + 1, lane);
       const int s = j % kStages, rs = j % kRopeSlots;
       bool ok = true;
@@ -480,24 +522,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0 && ok && j >= kRopeSlots) ok = waiter.wait(sh.bar(kBarRopeEmpty + rs), ((j / kRopeSlots) - 1) & 1);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      const int t0 = start + j * kTile;
-      const int live = min(nsub, (end - t0 + g - 1) / g);
-      if (lane == 0) mbar_arrive_expect_tx(sh.bar(kBarKvFull + s), (uint32_t)(live * g) * kRowBytes);
-      TMLA_TRACE(0, j);
-      if (lane == 0 && j == 0) TMLA_SPAN(2);
-      __syncwarp();
-      if (page_ok(j, lane, pg)) {
-        const int t = t0 + lane * g;
-        const int slot = p.block_table ? t % p.page_size : t;
-        const uint32_t dst = sh.stage(s);
-        const uint32_t bar = sh.bar(kBarKvFull + s);
-#pragma unroll
-        for (int kb = 0; kb < 4; ++kb)
-          tma_load_3d(dst + kb * kBoxBytes + lane * g * 128, &tm_kv_lat, bar, kHalfLatent * rank + 64 * kb, slot, pg,
-                      pol_stream);
-        tma_load_3d(sh.rope(rs) + lane * g * (kHalfRope * 2), &tm_kv_rope, bar, 512 + kHalfRope * rank, slot, pg,
-                    pol_stream);
-      }
+      issue_tile(j, pg);
       issued = j + 1;
     }
     // Drain: every issued load (the last ring stages and Q) has landed before the CTA may exit.
