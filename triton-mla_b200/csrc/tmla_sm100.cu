@@ -41,14 +41,25 @@
 // coordinates); warp 1: TMEM allocation and QK issue; warp 2: PV issue;
 // warp 3: forwards "score buffer read" signals to the peer.
 // Warps 4-15 work on TMEM lane quarter w % 4 (the only lanes a warp can reach),
-// one warp of each role per quarter, so every SM sub-partition runs one
-// softmax warp:
-//   warps 4-7    softmax of the 16 owned rows (4 threads per row, 16-lane TMEM
-//                access shapes), P to both CTAs' P buffers, O rescale
-//   warps 8-11   score senders: ship the peer-owned partial rows to the owner
-//   warps 12-15  wait for the peer's P rows, rescale O for them
-// O is rescaled lazily: only when a row maximum grows by more than 2^8.  The
-// output is written by warps 4-11, one thread per row.
+// one warp of each role per quarter:
+//   warps 4-7    softmax warpgroup A: tiles 0, 2, 4, ...
+//   warps 8-11   softmax warpgroup B: tiles 1, 3, 5, ...
+//   warps 12-15  score senders: ship the peer-owned partial rows to the owner
+// A softmax warpgroup takes its 16 owned rows per quarter (4 threads per row,
+// 16-lane TMEM access shapes), writes P to both CTAs' P buffers, rescales O for
+// those rows, then waits for the peer's P rows of the same tile and rescales O
+// for them when the peer asks.  The running maximum of tile j-1 reaches the
+// warpgroup of tile j through shared memory (one barrier per quarter); each
+// warpgroup keeps partial row sums relative to the maximum of its own last tile
+// and the two are combined at the end.  O is rescaled lazily: only when a row
+// maximum grows by more than 2^8.
+//
+// Prologue: the producer's barriers are initialised by its own lane 0, so the
+// first tile (page ids read speculatively at entry) and Q's RoPE half are
+// requested before the CTA-wide and cluster-wide syncs.  Epilogue: warpgroups A
+// and B stage O (scaled by 1/l) into 128B-swizzled tiles in the idle cache ring
+// and one thread writes them with TMA tensor stores (fp32 split partials, or the
+// final 16-bit output; rows past H lie outside the tensor map and are skipped).
 //
 // Every wait is bounded (2 s per wait, %globaltimer); on expiry the CTA sets
 // TMLA_STATUS_TIMEOUT, all roles leave their loops, in-flight copies and MMAs
