@@ -95,6 +95,31 @@ def make_workload(cfg, device, seed):
     return q, kv, lens.to(device), bt.to(device)
 
 
+def make_sharded_workload(cfg, device, seed, rank, world):
+    """One global ragged batch (the same lengths on every rank, from ``seed``) split over the
+    ranks by token count (longest first onto the least-loaded rank); this rank builds only
+    its own requests' q rows, page pool and block table.  Returns the rank's inputs and the
+    global token count and batch size."""
+    import torch
+    from triton_mla.sharding import balance_requests
+    gen_cpu = torch.Generator().manual_seed(seed)
+    lens_all = torch.randint(1, cfg["seqlen"] + 1, (cfg["batch"],), generator=gen_cpu, dtype=torch.int32)
+    reqs = balance_requests(lens_all.tolist(), world)[rank]
+    lens = lens_all[reqs]
+    need = (lens + PAGE - 1) // PAGE
+    num_pages = max(1, int(need.sum()))
+    g = torch.Generator(device=device).manual_seed(seed + 1 + rank)
+    kv = torch.randn(num_pages, PAGE, D_QK, generator=g, device=device, dtype=torch.bfloat16)
+    q = torch.randn(len(reqs), 128, D_QK, generator=g, device=device, dtype=torch.bfloat16)
+    perm = torch.randperm(num_pages, generator=gen_cpu)
+    bt = torch.zeros(len(reqs), max(1, int(need.max()) if len(reqs) else 1), dtype=torch.int32)
+    at = 0
+    for b, k in enumerate(need.tolist()):
+        bt[b, :k] = perm[at:at + k].int()
+        at += k
+    return q, kv, lens.to(device), bt.to(device), int(lens_all.sum()), cfg["batch"]
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle-reason samples every 50 ms while running."""
 
@@ -231,9 +256,18 @@ def main(argv=None):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     cfg = CONFIGS[args.config]
-    q, kv, lens, bt = make_workload(cfg, device, seed=1000 + rank)
+    # Uniform configs scale weakly (every rank decodes its own batch of the config); the
+    # ragged config scales strongly (one global batch, token-balanced over the ranks).
+    strong = bool(cfg["ragged"])
+    if strong:
+        q, kv, lens, bt, job_tokens, job_batch = make_sharded_workload(cfg, device, 1000, rank, world)
+    else:
+        q, kv, lens, bt = make_workload(cfg, device, seed=1000 + rank)
     B = q.shape[0]
     total_tokens = int(lens.sum())
+    if not strong:
+        job_tokens, job_batch = world * total_tokens, world * B
+    job_flops = decode_flops(job_tokens, 128)
     flops = decode_flops(total_tokens, 128)
     nbytes = decode_bytes(total_tokens, B, 128)
     splits = get_num_splits(B, 128, int(lens.max()), torch.cuda.get_device_properties(device).multi_processor_count)
@@ -377,7 +411,7 @@ def main(argv=None):
                          "(numpy oracle, fp32, BLAS threads = all host cores)"}
     line = {
         "metric": METRIC,
-        "value": world * flops / (ms_max * 1e-3) / 1e12,
+        "value": job_flops / (ms_max * 1e-3) / 1e12,
         "unit": "TFLOPS",
         "n_gpus": world,
         "steps": args.steps,
@@ -385,16 +419,19 @@ def main(argv=None):
         "ms_per_step": ms_max,
         "us_per_call": ms_max * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic N(0,1) (no dataset; BASELINE configs are synthetic)",
-        "config": {"workload": cfg["desc"], "batch_per_gpu": B, "heads": 128, "page_size": PAGE,
+        "config": {"workload": cfg["desc"], "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
+                   "page_size": PAGE, "tokens_per_job": job_tokens,
                    "tokens_per_gpu": total_tokens, "num_splits": splits, "kernel": kname,
-                   "l2": "flushed (256 MiB write) before every timed step", "parallelism": f"dp{world} (batch-sharded)"},
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": (f"dp{world} (token-balanced request shards of one batch, own page pools)" if strong
+                                   else f"dp{world} (each rank its own batch and page pool)")},
         "roofline": roofline,
         "cpu_baseline": cpu,
-        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": e2e_ms,
+        "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "per step: q, seqlens, block_table host->device; out, lse device->host; cache resident"},
         "gpu_launches": gpu_launches,
