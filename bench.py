@@ -13,6 +13,10 @@ independent, so every rank decodes its own batch from its own page pool; there
 is no collective on the data path (NCCL only for barriers and the max-over-ranks
 timing).  Scaling is weak: per-GPU work is fixed.
 
+``--config cfg5`` times one decode step of the full MLA layer instead (BASELINE
+config 5: DeepSeek-V3 dims, random-init weights, 16 requests per GPU with 8192
+cached tokens, weights replicated on every rank).
+
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 numpy oracle) on the host cores on a bounded sample of the same workload.
 """
@@ -46,6 +50,10 @@ CONFIGS = {
                  batch=4, seqlen=65536, ragged=False),
     "cfg4": dict(desc="BASELINE config 4: B=256 H=128 S~U[1,16384] page 64 bf16, pages from one shared pool",
                  batch=256, seqlen=16384, ragged=True),
+    "cfg5": dict(desc="BASELINE config 5: MLA layer decode step, DeepSeek-V3 dims (hidden 7168, q_lora 1536, "
+                      "kv_lora 512, nope 128, rope 64, v 128, H=128), 16 requests per GPU x 8192 cached tokens, "
+                      "page 64, bf16, random-init weights N(0,0.02)",
+                 batch=16, seqlen=8192, ragged=False, layer=True),
 }
 
 
@@ -118,6 +126,176 @@ def make_sharded_workload(cfg, device, seed, rank, world):
         bt[b, :k] = perm[at:at + k].int()
         at += k
     return q, kv, lens.to(device), bt.to(device), int(lens_all.sum()), cfg["batch"]
+
+
+def layer_counts(batch, context):
+    """Algorithmic FLOPs and bytes of one MLA layer decode step (DeepSeek-V3 dims, bf16):
+    the projections wq_a, wq_b, wkv_a, wo and the absorption by W_UK / W_UV read every
+    weight once (2 FLOPs per weight and request), plus the decode over context + 1 tokens."""
+    hid, qr, h, r = 7168, 1536, 128, 512
+    linear = hid * qr + qr * h * 192 + hid * (r + 64) + h * 128 * hid
+    absorb = 2 * h * 128 * r
+    tokens = batch * (context + 1)
+    flops = 2.0 * batch * (linear + absorb) + decode_flops(tokens, h)
+    nbytes = 2.0 * (linear + absorb) + decode_bytes(tokens, batch, h) + 2.0 * 2 * batch * hid
+    return flops, nbytes
+
+
+def run_layer(args, cfg, device, world, rank, local):
+    """--config cfg5: one MLA layer decode step per timed step (weak scaling: every rank holds
+    the weights and its own 16 requests)."""
+    import torch
+    import torch.distributed as dist
+    from triton_mla import MLA, MLAConfig, MLADecodeGraph, get_num_splits
+    torch.manual_seed(1000 + rank)
+    mcfg = MLAConfig()
+    layer = MLA(mcfg)
+    with torch.no_grad():
+        for name, prm in layer.named_parameters():
+            if "norm" in name:
+                prm.fill_(1.0)
+            else:
+                prm.normal_(0.0, 0.02)
+    layer = layer.to(device=device, dtype=torch.bfloat16)
+    B, ctx = cfg["batch"], cfg["seqlen"]
+    need = (ctx + 1 + PAGE - 1) // PAGE
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    kv = torch.randn(B * need, PAGE, D_QK, generator=g, device=device, dtype=torch.bfloat16)
+    bt = torch.randperm(B * need, generator=torch.Generator().manual_seed(rank)).view(B, need).int().to(device)
+    lens = torch.full((B,), ctx, dtype=torch.int32, device=device)
+    x = torch.randn(B, mcfg.hidden_size, generator=g, device=device, dtype=torch.bfloat16)
+    splits = get_num_splits(B, 128, ctx + 1, torch.cuda.get_device_properties(device).multi_processor_count)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    flops, nbytes = layer_counts(B, ctx)
+
+    @torch.no_grad()
+    def eager_step(xin):
+        # the new token is written at position ctx every step, so the work per step is fixed
+        out, _ = layer(xin, kv, lens, bt, num_splits=splits)
+        return out
+
+    # The timed step is the layer step captured in a CUDA graph (one launch per step).
+    graph = MLADecodeGraph(layer, kv, lens, bt, num_splits=splits)
+
+    def step(xin):
+        return graph(xin)
+
+    for _ in range(args.warmup):
+        step(x)
+        eager_step(x)
+    torch.cuda.synchronize()
+    eager = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        eager_step(x)
+        b.record(stream)
+        eager.append((a, b))
+    torch.cuda.synchronize()
+    eager_us = 1e3 * sum(a.elapsed_time(b) for a, b in eager) / len(eager)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < args.clock_soak:
+            for _ in range(8):
+                flush.zero_()
+                step(x)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step(x)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # end to end: x from pinned host memory in, the layer output back to the host
+    x_h = x.cpu().pin_memory()
+    out_h = torch.empty(B, mcfg.hidden_size, dtype=torch.bfloat16).pin_memory()
+    e_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        out_h.copy_(step(x_h.to(device, non_blocking=True)), non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if i >= args.warmup:
+            e_ms.append(a.elapsed_time(b))
+    te = torch.tensor([sum(e_ms) / len(e_ms)], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    hbm, tflops_peak, peak_kind = peaks()
+    t_bytes, t_flops = nbytes / (hbm * 1e9), flops / (tflops_peak * 1e12)
+    bound = "hbm" if t_bytes >= t_flops else "tensor"
+    achieved = (nbytes / (ms * 1e-3) / 1e9) if bound == "hbm" else (flops / (ms * 1e-3) / 1e12)
+    peak = hbm if bound == "hbm" else tflops_peak
+    cpu = None
+    if world == 1 and args.cpu_budget > 0:
+        cpu = cpu_layer_rate(layer, kv, bt, ctx, min(args.cpu_budget, 20.0))
+    line = {
+        "metric": METRIC, "value": world * flops / (ms_max * 1e-3) / 1e12, "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "us_per_call": ms_max * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1) cache and input, random-init weights (no checkpoint, no dataset)",
+        "config": {"workload": cfg["desc"], "batch_per_gpu": B, "global_batch": world * B, "context": ctx,
+                   "num_splits": splits, "step": "MLADecodeGraph (the layer step captured in one CUDA graph)",
+                   "eager_us_per_step": eager_us, "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": f"dp{world} (weights replicated, each rank its own requests and page pool)"},
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "traffic_source": "not captured for this config",
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
+                     "kernel": "whole layer step (cuBLAS projections + tcgen05 decode)",
+                     "algorithmic_bytes_per_step": nbytes, "algorithmic_flops_per_step": flops},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * flops / (float(te.item()) * 1e-3) / 1e12, "unit": "TFLOPS",
+                "ms_per_step": float(te.item()), "h2d_bytes_per_step": x_h.numel() * 2,
+                "d2h_bytes_per_step": out_h.numel() * 2,
+                "note": "per step: x host->device, layer output device->host; weights and cache resident"},
+        "gpu_launches": args.steps * (1 + (1 if splits > 1 else 0)),
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_layer_rate(layer, kv, bt, ctx, budget_s):
+    """The numpy layer oracle (absorbed form, fp64) on one request of the workload, timed on
+    the host cores for about ``budget_s`` seconds."""
+    import numpy as np
+    from oracle import mla_oracle as orc
+    w = {k: v.float().cpu().numpy() for k, v in layer.state_dict().items()}
+    w = {k.replace(".weight", ""): v for k, v in w.items()}
+    ocfg = dict(hidden_size=7168, num_heads=128, q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=128,
+                qk_rope_head_dim=64, v_head_dim=128, rope_theta=10000.0, rms_norm_eps=1e-6)
+    need = bt.shape[1]
+    pages = bt[0].long().cpu()
+    kv1 = kv.index_select(0, pages.to(kv.device)).float().cpu().numpy()
+    bt1 = np.arange(need, dtype=np.int32)[None]
+    x = np.random.default_rng(0).standard_normal((1, 7168)).astype(np.float32)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or done == 0:
+        orc.mla_layer_forward_absorbed(w, ocfg, x, kv1, np.array([ctx]), bt1)
+        done += 1
+    el = time.perf_counter() - t0
+    flops, _ = layer_counts(1, ctx)
+    return {"value": done * flops / el / 1e12, "unit": "TFLOPS", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{done} layer steps of 1 request x {ctx} tokens in {el:.1f}s "
+                      "(numpy layer oracle, fp64, BLAS threads = all host cores)"}
 
 
 class ClockSampler:
@@ -256,6 +434,8 @@ def main(argv=None):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     cfg = CONFIGS[args.config]
+    if cfg.get("layer"):
+        return run_layer(args, cfg, device, world, rank, local)
     # Uniform configs scale weakly (every rank decodes its own batch of the config); the
     # ragged config scales strongly (one global batch, token-balanced over the ranks).
     strong = bool(cfg["ragged"])

@@ -186,6 +186,34 @@ def test_strided_out_view_and_partial_head_tile(device, num_splits):
     assert read_status(device) == 0
 
 
+def test_cuda_graph_capture_with_default_splits(device):
+    """mla_decode(num_splits=None) captured in a CUDA graph (no host sync inside capture)
+    and replayed after the lengths and the query changed in place."""
+    case = recipes.paged_case([300, 4096, 17, 1000], 128, 64, seed=41)
+    c = to_dev(case, device)
+    q, lens, bt, kv = c["q"].clone(), c["seqlens"].clone(), c["block_table"], c["kv"]
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):  # warm-up outside the capture, as torch.cuda.graphs asks
+        mla_decode(q, kv, lens, bt, softmax_scale=c["scale"], return_lse=True)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out, lse = mla_decode(q, kv, lens, bt, softmax_scale=c["scale"], return_lse=True)
+    g = torch.Generator().manual_seed(42)
+    for new_lens in ([300, 4096, 17, 1000], [4096, 1, 0, 2500], [64, 65, 4000, 3]):
+        q_new = torch.randn(q.shape, generator=g).to(q.dtype)
+        q.copy_(q_new.to(device))
+        lens.copy_(torch.tensor(new_lens, dtype=torch.int32, device=device))
+        graph.replay()
+        torch.cuda.synchronize(device)
+        sub = dict(case, q=q_new, seqlens=torch.tensor(new_lens, dtype=torch.int32))
+        ref_out, ref_lse = oracle_of(sub)
+        check(out, lse, ref_out, ref_lse, new_lens)
+        assert read_status(device) == 0
+    del graph
+
+
 def test_empty_batch(device):
     q = torch.zeros(0, 128, 576, dtype=torch.bfloat16, device=device)
     kv = torch.zeros(4, 64, 576, dtype=torch.bfloat16, device=device)

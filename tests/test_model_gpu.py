@@ -9,7 +9,7 @@ import torch
 import recipes
 from conftest import load_golden
 from oracle import mla_oracle as orc
-from triton_mla import MLA, MLAConfig
+from triton_mla import MLA, MLAConfig, MLADecodeGraph
 
 pytestmark = pytest.mark.gpu
 
@@ -89,3 +89,29 @@ def test_deepseek_v3_layer_step_against_oracle(device):
     got = out.float().cpu().numpy()
     scale = np.abs(ref).max()
     assert np.abs(got - ref).max() <= 3e-2 * max(scale, 1.0)
+
+
+def test_decode_step_graph_matches_eager(device):
+    """MLADecodeGraph replays MLA.forward: same output and appended cache rows as the eager
+    step, following the lengths written in place between replays."""
+    inp = recipes.layer_inputs(True, seed=6)
+    model = _model(device, torch.bfloat16)
+    bt = inp["block_table"].to(device)
+    lens0 = inp["seqlens"].to(device)
+    kv_eager = inp["kv"].to(device, torch.bfloat16)
+    kv_graph = kv_eager.clone()
+    lens_graph = lens0.clone()  # the length tensor the graph reads at every replay
+    step = MLADecodeGraph(model, kv_graph, lens_graph, bt, num_splits=2)
+    kv_graph.copy_(kv_eager)  # undo the warm-up step run before the capture
+    g = torch.Generator().manual_seed(7)
+    for i in range(3):
+        x = torch.randn(inp["x"].shape, generator=g).to(device, torch.bfloat16)
+        cur = lens0 + i
+        with torch.no_grad():
+            ref, ref_next = model(x, kv_eager, cur, bt, num_splits=2)
+        lens_graph.copy_(cur)
+        out = step(x)
+        torch.cuda.synchronize(device)
+        torch.testing.assert_close(out.float(), ref.float(), atol=3e-2, rtol=3e-2)
+        assert torch.equal(step.next_seqlens, ref_next)
+        torch.testing.assert_close(kv_graph.float(), kv_eager.float(), atol=1e-2, rtol=1e-2)

@@ -6,7 +6,7 @@ Exports the same names as the reference package (src/triton_mla/__init__.py:1-14
 """
 
 from .kernel import get_num_splits, mla_decode, read_status, selected_kernel
-from .model import MLA, MLAConfig
+from .model import MLA, MLAConfig, MLADecodeGraph
 from .reference import mla_decode_ref, mla_decode_torch
 
 __version__ = "0.1.1"
@@ -14,6 +14,7 @@ __version__ = "0.1.1"
 __all__ = [
     "MLA",
     "MLAConfig",
+    "MLADecodeGraph",
     "get_num_splits",
     "mla_decode",
     "mla_decode_ref",

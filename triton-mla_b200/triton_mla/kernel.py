@@ -9,7 +9,11 @@ reference's ``triton_mla.mla_decode`` (src/triton_mla/kernel.py:204-323):
 * ``softmax_scale`` defaults to ``d_qk ** -0.5`` (kernel.py:247-248);
 * ``block_table is None`` selects the dense ``[B, S_max, D]`` layout (kernel.py:257-262);
 * ``num_splits=None`` costs one host sync to read the longest request
-  (kernel.py:264-266); an explicit value keeps the call sync-free (CUDA-graph safe);
+  (kernel.py:264-266); an explicit value keeps the call sync-free (CUDA-graph safe).
+  Inside CUDA-graph capture, where the reference's sync would fail, ``None`` sizes the
+  split count for the longest request the cache can hold (no sync): the kernels read
+  the actual lengths on the device, so the captured call stays valid when the lengths
+  change between replays;
 * returns ``out [B, H, head_dim_v]`` in ``q.dtype`` and, with ``return_lse``,
   the natural-log LSE ``[B, H]`` fp32; zero-length requests give 0 and -inf.
 
@@ -179,7 +183,11 @@ def mla_decode(
 
     device = q.device
     if num_splits is None:
-        max_seqlen = int(cache_seqlens.max().item()) if batch > 0 else 0
+        if batch > 0 and torch.cuda.is_current_stream_capturing():
+            # No host sync during capture: size the splits for the longest request the cache holds.
+            max_seqlen = bt_width * page_size if paged else kv_cache.shape[1]
+        else:
+            max_seqlen = int(cache_seqlens.max().item()) if batch > 0 else 0
         num_splits = get_num_splits(batch, num_heads, max_seqlen, _num_sms(device))
     num_splits = int(num_splits)
 
@@ -219,7 +227,7 @@ def mla_decode(
     finally:
         if prev != device.index:
             torch.cuda.set_device(prev)
-    if _CHECK:
+    if _CHECK and not torch.cuda.is_current_stream_capturing():
         st = read_status(device)
         if st:
             raise RuntimeError(f"mla_decode device status 0x{st:x} (bad page id / length, or a wait timed out)")

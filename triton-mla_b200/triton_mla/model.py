@@ -138,3 +138,38 @@ class MLA(nn.Module):
         probs = logits.masked_fill(invalid[:, None, :], float("-inf")).softmax(-1)
         o = torch.einsum("bhs,bshd->bhd", probs, v.float()).to(x.dtype)
         return self.wo(o.flatten(1)), seqlens
+
+
+class MLADecodeGraph:
+    """One ``MLA.forward`` decode step captured in a CUDA graph for fixed shapes.
+
+    The projections, norms, RoPE, cache append, absorption, decode kernels and output
+    projection replay as one graph launch, so a step costs no per-op launch or Python
+    time.  The graph reads the new tokens from ``self.x`` (or the ``x`` given to the
+    call, copied there) and the lengths from ``cache_seqlens`` as they are at replay
+    time (update it in place between steps), appends to ``kv_cache`` in place and
+    writes ``self.out`` [batch, hidden] and ``self.next_seqlens`` (= lengths + 1).
+    ``num_splits=None`` is sized at capture for the longest request the cache holds.
+    No counterpart in the reference, which runs the step eagerly.
+    """
+
+    def __init__(self, layer: MLA, kv_cache, cache_seqlens, block_table=None, num_splits=None):
+        param = next(layer.parameters())
+        batch = cache_seqlens.shape[0]
+        self.x = torch.zeros(batch, layer.cfg.hidden_size, dtype=param.dtype, device=param.device)
+        self.graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(param.device)
+        side.wait_stream(torch.cuda.current_stream(param.device))
+        with torch.no_grad(), torch.cuda.stream(side):
+            layer(self.x, kv_cache, cache_seqlens, block_table, num_splits=num_splits)  # warm-up outside capture
+        torch.cuda.current_stream(param.device).wait_stream(side)
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.out, self.next_seqlens = layer(self.x, kv_cache, cache_seqlens, block_table, num_splits=num_splits)
+
+    def __call__(self, x=None):
+        """Replay the step (after copying ``x`` into the graph's input when given); returns ``self.out``."""
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.out
+
