@@ -146,6 +146,68 @@ int tmla_abi_version(void);
 /* sizeof(TmlaDecodeParams) as compiled, so an FFI binding can check its mirror of the struct. */
 size_t tmla_params_bytes(void);
 
+/* ---------------------------------------------------------------- MLA layer step, fused
+   The small operations of one MLA layer decode step around the decode itself, one
+   launch each (the reference runs them as PyTorch ops in MLA.forward,
+   src/triton_mla/model.py:74-94 and 111-123).  dtype is TMLA_DTYPE_*; all tensors
+   of one call share it.  w_kv_b is wkv_b.weight, [heads * (d_nope + d_v), rank]
+   row-major: head h's W_UK is rows [h (d_nope + d_v), + d_nope), its W_UV the next
+   d_v rows.  RoPE is the reference's half-split form at the given positions. */
+
+/* q_out[b, h, :] = [ q_in[b, h, :d_nope] . W_UK[h]  |  rope(q_in[b, h, d_nope:], positions[b]) ]:
+   the decode query from wq_b's output (model.py:111-113 with the q_pe RoPE of model.py:78).
+   Needs rank even and w_kv_b 8-byte aligned (else TMLA_ERR_MISALIGNED); d_nope <= 512. */
+typedef struct TmlaQPrepParams {
+  const void* q_in;                /* [batch, heads, d_nope + d_rope] */
+  int64_t q_in_stride_b, q_in_stride_h;
+  const void* w_kv_b;
+  const int32_t* positions;        /* [batch]: the new token's position (cache length before the append) */
+  void* q_out;                     /* [batch, heads, rank + d_rope] */
+  int64_t q_out_stride_b, q_out_stride_h;
+  int32_t batch, num_heads, d_nope, d_rope, d_v, rank;
+  int32_t dtype;
+  float rope_theta;
+} TmlaQPrepParams;
+int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream);
+
+/* The new token's cache row [ rmsnorm(kv_in[b, :rank]) * norm_weight | rope(kv_in[b, rank:]) ]
+   written at position positions[b] of request b (paged through block_table, or dense
+   [batch, page_size, rank + d_rope] when block_table is NULL), and seqlens_out[b] =
+   positions[b] + 1 when seqlens_out is not NULL (model.py:74-94, 116-117).  A position
+   past the cache or a page id outside the pool sets TMLA_STATUS_BAD_PAGE and drops the row. */
+typedef struct TmlaKvAppendParams {
+  const void* kv_in;               /* [batch, rank + d_rope]: wkv_a's output */
+  int64_t kv_in_stride_b;
+  const void* norm_weight;         /* [rank] */
+  const int32_t* positions;        /* [batch] */
+  int32_t* seqlens_out;            /* [batch] or NULL */
+  void* kv_cache;                  /* pages [num_pages, page_size, rank + d_rope] */
+  int64_t kv_stride_page, kv_stride_tok, num_pages;
+  int32_t page_size;
+  const int32_t* block_table;      /* [batch, bt_width] or NULL */
+  int64_t bt_stride;
+  int32_t bt_width;
+  int32_t* status;                 /* optional device status word */
+  int32_t batch, rank, d_rope;
+  int32_t dtype;
+  float eps, rope_theta;
+} TmlaKvAppendParams;
+int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream);
+
+/* out[b, h * d_v + d] = sum_c o[b, h, c] W_UV[h][d][c]: the decode output projected back per
+   head, the input of wo (model.py:123).  Needs rank a multiple of 16 (<= 2048) and w_kv_b
+   16-byte aligned (else TMLA_ERR_MISALIGNED). */
+typedef struct TmlaOUnabsorbParams {
+  const void* o;                   /* [batch, heads, rank]: mla_decode's output */
+  int64_t o_stride_b, o_stride_h;
+  const void* w_kv_b;
+  void* out;                       /* [batch, heads * d_v] */
+  int64_t out_stride_b;
+  int32_t batch, num_heads, d_nope, d_v, rank;
+  int32_t dtype;
+} TmlaOUnabsorbParams;
+int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

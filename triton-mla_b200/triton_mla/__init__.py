@@ -5,6 +5,7 @@ Exports the same names as the reference package (src/triton_mla/__init__.py:1-14
 ``libtriton_mla_b200.so``; there is no Triton and no CPU implementation.
 """
 
+from . import layer_ops, sharding
 from .kernel import get_num_splits, mla_decode, read_status, selected_kernel
 from .model import MLA, MLAConfig, MLADecodeGraph
 from .reference import mla_decode_ref, mla_decode_torch

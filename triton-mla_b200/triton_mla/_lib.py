@@ -52,6 +52,9 @@ EXPORTED = (
     "tmla_last_cuda_error",
     "tmla_abi_version",
     "tmla_params_bytes",
+    "tmla_q_absorb_rope",
+    "tmla_kv_norm_rope_append",
+    "tmla_o_unabsorb",
 )
 
 
@@ -88,6 +91,75 @@ class TmlaDecodeParams(ctypes.Structure):
         ("kernel", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float),
+    ]
+
+
+class TmlaQPrepParams(ctypes.Structure):
+    """Mirror of ``TmlaQPrepParams``."""
+
+    _fields_ = [
+        ("q_in", ctypes.c_void_p),
+        ("q_in_stride_b", ctypes.c_int64),
+        ("q_in_stride_h", ctypes.c_int64),
+        ("w_kv_b", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("q_out", ctypes.c_void_p),
+        ("q_out_stride_b", ctypes.c_int64),
+        ("q_out_stride_h", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("d_nope", ctypes.c_int32),
+        ("d_rope", ctypes.c_int32),
+        ("d_v", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("rope_theta", ctypes.c_float),
+    ]
+
+
+class TmlaKvAppendParams(ctypes.Structure):
+    """Mirror of ``TmlaKvAppendParams``."""
+
+    _fields_ = [
+        ("kv_in", ctypes.c_void_p),
+        ("kv_in_stride_b", ctypes.c_int64),
+        ("norm_weight", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("seqlens_out", ctypes.c_void_p),
+        ("kv_cache", ctypes.c_void_p),
+        ("kv_stride_page", ctypes.c_int64),
+        ("kv_stride_tok", ctypes.c_int64),
+        ("num_pages", ctypes.c_int64),
+        ("page_size", ctypes.c_int32),
+        ("block_table", ctypes.c_void_p),
+        ("bt_stride", ctypes.c_int64),
+        ("bt_width", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("d_rope", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+    ]
+
+
+class TmlaOUnabsorbParams(ctypes.Structure):
+    """Mirror of ``TmlaOUnabsorbParams``."""
+
+    _fields_ = [
+        ("o", ctypes.c_void_p),
+        ("o_stride_b", ctypes.c_int64),
+        ("o_stride_h", ctypes.c_int64),
+        ("w_kv_b", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_stride_b", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("d_nope", ctypes.c_int32),
+        ("d_v", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
     ]
 
 
@@ -140,6 +212,11 @@ def load() -> ctypes.CDLL:
     lib.tmla_abi_version.restype = ctypes.c_int
     lib.tmla_params_bytes.argtypes = []
     lib.tmla_params_bytes.restype = ctypes.c_size_t
+    for name, st in (("tmla_q_absorb_rope", TmlaQPrepParams), ("tmla_kv_norm_rope_append", TmlaKvAppendParams),
+                     ("tmla_o_unabsorb", TmlaOUnabsorbParams)):
+        fn = getattr(lib, name)
+        fn.argtypes = [ctypes.POINTER(st), vp]
+        fn.restype = ctypes.c_int
     if lib.tmla_abi_version() != ABI_VERSION:
         raise ImportError(f"{path}: ABI version {lib.tmla_abi_version()} != {ABI_VERSION}; rebuild it")
     if lib.tmla_params_bytes() != ctypes.sizeof(TmlaDecodeParams):

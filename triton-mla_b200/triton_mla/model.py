@@ -9,8 +9,12 @@ num_splits=None) -> (out, seqlens)`` appends the new token in place and runs
 the absorbed decode (model.py:101-124); ``MLA.forward_naive`` is the
 decompressed form (model.py:126-144).
 
-The attention step is ``mla_decode`` (CUDA library).  The projections,
-norms, RoPE, cache append and the absorption einsums stay PyTorch (cuBLAS).
+The attention step is ``mla_decode`` (CUDA library).  The projections are
+cuBLAS GEMMs (``nn.Linear``) and q_norm is PyTorch's RMSNorm; the rest of a
+decode step runs as three fused CUDA launches (``layer_ops``): the kv_norm,
+k_pe RoPE and cache append; the q_pe RoPE, absorption by W_UK and concatenation
+into the decode query; and the W_UV projection of the decode output.  Steps
+whose tensors do not share one dtype take the PyTorch-op form of the same math.
 """
 
 from __future__ import annotations
@@ -21,6 +25,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import layer_ops
 from .kernel import mla_decode
 from .reference import gather_kv
 
@@ -110,6 +115,32 @@ class MLA(nn.Module):
 
     def forward(self, x, kv_cache, cache_seqlens, block_table=None, num_splits=None):
         """One decode step for x [batch, hidden]; returns (out [batch, hidden], cache_seqlens + 1)."""
+        cfg = self.cfg
+        weights = (self.wq_a.weight, self.q_norm.weight, self.wq_b.weight, self.wkv_a.weight, self.kv_norm.weight,
+                   self.wkv_b.weight, self.wo.weight)
+        if layer_ops.fusable(x, kv_cache, weights, cfg.kv_lora_rank, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim):
+            return self._forward_fused(x, kv_cache, cache_seqlens, block_table, num_splits)
+        return self._forward_ops(x, kv_cache, cache_seqlens, block_table, num_splits)
+
+    def _forward_fused(self, x, kv_cache, cache_seqlens, block_table, num_splits):
+        cfg = self.cfg
+        batch = x.shape[0]
+        q = self.wq_b(self.q_norm(self.wq_a(x))).view(batch, cfg.num_heads, cfg.qk_head_dim)
+        kva = self.wkv_a(x)
+        positions = cache_seqlens.to(torch.int32).contiguous()
+        bt = None if block_table is None else block_table.to(torch.int32).contiguous()
+        seqlens = torch.empty_like(positions)
+        layer_ops.kv_norm_rope_append(kva, self.kv_norm.weight, positions, kv_cache, bt, self.kv_norm.eps,
+                                      cfg.rope_theta, seqlens_out=seqlens)
+        q_full = layer_ops.q_absorb_rope(q, self.wkv_b.weight, positions, cfg.qk_nope_head_dim, cfg.v_head_dim,
+                                         cfg.rope_theta)
+        o = mla_decode(q_full, kv_cache, seqlens, bt, head_dim_v=cfg.kv_lora_rank, softmax_scale=self.softmax_scale,
+                       num_splits=num_splits)
+        o = layer_ops.o_unabsorb(o, self.wkv_b.weight, cfg.qk_nope_head_dim, cfg.v_head_dim)
+        return self.wo(o), seqlens.to(cache_seqlens.dtype)
+
+    def _forward_ops(self, x, kv_cache, cache_seqlens, block_table, num_splits):
+        """The decode step as PyTorch ops around ``mla_decode`` (mixed dtypes)."""
         q_nope, q_pe, c_kv, k_pe = self._project(x, cache_seqlens)
         self._append_kv(kv_cache, c_kv, k_pe, cache_seqlens, block_table)
         seqlens = cache_seqlens + 1
