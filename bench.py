@@ -421,7 +421,7 @@ def main(argv=None):
 
     import torch
     import torch.distributed as dist
-    from triton_mla import _lib, get_num_splits, mla_decode
+    from triton_mla import _lib, get_num_splits, make_split_plan, mla_decode
     from triton_mla.kernel import _DTYPE_CODES, _KERNELS, _status_word, selected_kernel
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -452,12 +452,15 @@ def main(argv=None):
     nbytes = decode_bytes(total_tokens, B, 128)
     splits = get_num_splits(B, 128, int(lens.max()), torch.cuda.get_device_properties(device).multi_processor_count)
     kname = selected_kernel(q, kv, bt, num_splits=splits, kernel=args.kernel)
+    # A ragged batch follows a per-request split plan, made once outside the timed region
+    # (it stays valid for any lengths of the batch); uniform batches use one split count.
+    plan = make_split_plan(lens, 128) if (cfg["ragged"] and kname == "sm100") else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
     def step():
         return mla_decode(q, kv, lens, bt, softmax_scale=SCALE, num_splits=splits, return_lse=True,
-                          kernel=args.kernel)
+                          kernel=args.kernel, plan=plan)
 
     for _ in range(args.warmup):
         step()
@@ -498,8 +501,14 @@ def main(argv=None):
     lib = _lib.load()
     lse = torch.empty(B, 128, dtype=torch.float32, device=device)
     out = torch.empty(B, 128, D_V, dtype=torch.bfloat16, device=device)
-    ws = torch.empty(max(lib.tmla_workspace_bytes(B, 128, max(splits, 2), D_V), 1), dtype=torch.uint8, device=device)
-    o_bytes = (B * 128 * max(splits, 2) * D_V * 4 + 255) & ~255
+    if plan is None:
+        ws = torch.empty(max(lib.tmla_workspace_bytes(B, 128, max(splits, 2), D_V), 1), dtype=torch.uint8,
+                         device=device)
+        o_bytes = (B * 128 * max(splits, 2) * D_V * 4 + 255) & ~255
+    else:
+        ws = torch.empty(max(lib.tmla_units_workspace_bytes(plan.num_slots, 128, D_V), 1), dtype=torch.uint8,
+                         device=device)
+        o_bytes = (plan.num_slots * 128 * D_V * 4 + 255) & ~255
     p = _lib.TmlaDecodeParams(
         q.data_ptr(), q.stride(0), q.stride(1), kv.data_ptr(), kv.stride(0), kv.stride(1), kv.shape[0], PAGE,
         lens.data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1], out.data_ptr(), out.stride(0), out.stride(1),
@@ -511,7 +520,12 @@ def main(argv=None):
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        _lib.check(lib.tmla_decode_partial(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "partial")
+        if plan is None:
+            _lib.check(lib.tmla_decode_partial(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "partial")
+        else:  # the plan's split kernel and its merge of the split requests, through the C ABI
+            _lib.check(lib.tmla_decode_units(ctypes.byref(p), plan.units.data_ptr(), plan.req_first.data_ptr(),
+                                             plan.num_units, plan.num_slots, ctypes.c_void_p(stream.cuda_stream)),
+                       "units")
         b.record(stream)
         if i >= args.warmup:
             ks.append(a)
@@ -533,7 +547,7 @@ def main(argv=None):
         ld = lens_h.to(device, non_blocking=True)
         bd = bt_h.to(device, non_blocking=True)
         o, l = mla_decode(qd, kv, ld, bd, softmax_scale=SCALE, num_splits=splits, return_lse=True,
-                          kernel=args.kernel)
+                          kernel=args.kernel, plan=plan)
         out_h.copy_(o, non_blocking=True)
         lse_h.copy_(l, non_blocking=True)
 
@@ -605,7 +619,10 @@ def main(argv=None):
         "data": "synthetic N(0,1) (no dataset; BASELINE configs are synthetic)",
         "config": {"workload": cfg["desc"], "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
                    "page_size": PAGE, "tokens_per_job": job_tokens,
-                   "tokens_per_gpu": total_tokens, "num_splits": splits, "kernel": kname,
+                   "tokens_per_gpu": total_tokens,
+                   "num_splits": splits if plan is None else
+                   f"per-request plan: {plan.num_units} units, {plan.num_slots} partial slots",
+                   "kernel": kname,
                    "l2": "flushed (256 MiB write) before every timed step",
                    "parallelism": (f"dp{world} (token-balanced request shards of one batch, own page pools)" if strong
                                    else f"dp{world} (each rank its own batch and page pool)")},

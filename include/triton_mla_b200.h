@@ -116,6 +116,30 @@ int tmla_decode(const TmlaDecodeParams* p, void* stream);
 #define TMLA_NOALLOC_SCRATCH_BYTES (32u << 20)
 int tmla_decode_noalloc(const TmlaDecodeParams* p, void* stream);
 
+/* Per-request split plan for ragged batches.  No counterpart in the reference, whose split
+   count is one number for the whole batch (kernel.py:190-201, 264-266).  From the request
+   lengths (host memory) it picks how many splits each request gets, so that the tcgen05
+   kernel's 2-CTA clusters, scheduled longest unit first, finish together: it simulates
+   longest-first scheduling of each candidate plan on num_sms / 2 clusters and keeps the
+   shortest.  Output, for up to max_units work units (batch * 64 always suffices):
+     units[4u .. 4u+3] = {request, split, splits of that request, partial slot or -1},
+     longest unit first; a request with one split has slot -1 and writes its output itself;
+     req_first[b] = first partial slot of request b, req_first[batch] = slots in all.
+   Returns the number of units, or -TMLA_ERR_INVALID_ARG.  Host-only: touches no GPU. */
+int32_t tmla_plan_units(const int32_t* seqlens, int32_t batch, int32_t num_heads, int32_t num_sms,
+                        int32_t max_units, int32_t* units, int32_t* req_first);
+
+/* Workspace of a plan with num_slots partial slots: ws_o = [num_slots, num_heads, d_v] fp32 at
+   its start, ws_lse = [num_slots, num_heads] fp32 at the next 256-byte boundary. */
+size_t tmla_units_workspace_bytes(int32_t num_slots, int32_t num_heads, int32_t d_v);
+
+/* Whole decode following a plan from tmla_plan_units (units and req_first copied to device
+   memory; p->num_splits is ignored): one cluster per unit and head tile, then the merge of
+   the split requests.  tcgen05 kernel only (TMLA_ERR_UNSUPPORTED for other shapes).  No
+   counterpart in the reference (see tmla_plan_units). */
+int tmla_decode_units(const TmlaDecodeParams* p, const int32_t* units, const int32_t* req_first,
+                      int32_t num_units, int32_t num_slots, void* stream);
+
 /* Stage 1 only: writes ws_o / ws_lse for every (request, head, split).
    Replaces the `_mla_decode_stage1` launch (kernel.py:276-302). */
 int tmla_decode_partial(const TmlaDecodeParams* p, void* stream);

@@ -136,3 +136,69 @@ def test_selected_kernel_reports_generic_for_non_deepseek_dims_on_cpu_tensors():
     q = torch.zeros(2, 16, 256 + 32, dtype=torch.bfloat16)
     kv = torch.zeros(2, 64, 256 + 32, dtype=torch.bfloat16)
     assert selected_kernel(q, kv, head_dim_v=256) == "generic"
+
+
+# ----------------------------------------------------------------------------- per-request split plan
+def _check_plan(lens, units, req_first):
+    import numpy as np
+    lens = np.asarray(lens)
+    tiles = (np.maximum(lens, 0) + 63) // 64
+    seen = {}
+    for b, s, ns, slot in units.tolist():
+        assert 1 <= ns <= 64 and 0 <= s < ns
+        assert (b, s) not in seen
+        seen[(b, s)] = ns
+        if ns == 1:
+            assert slot == -1
+        else:
+            assert slot == req_first[b] + s
+    for b in range(len(lens)):
+        ns = seen[(b, 0)]
+        assert all(seen[(b, s)] == ns for s in range(ns))
+        assert req_first[b + 1] - req_first[b] == (ns if ns > 1 else 0)
+    # longest unit first (tiles of each split as split_range cuts them)
+    sizes = []
+    for b, s, ns, _ in units.tolist():
+        per = -(-int(tiles[b]) // ns)
+        sizes.append(max(0, min(int(tiles[b]), (s + 1) * per) - min(int(tiles[b]), s * per)))
+    assert sizes == sorted(sizes, reverse=True)
+
+
+def test_plan_units_reproduces_uniform_splits_for_uniform_batches():
+    from triton_mla.kernel import plan_units
+    units, first = plan_units([4096] * 32, 128, 148)
+    assert set(units[:, 2].tolist()) == {2} and len(units) == 64
+    _check_plan([4096] * 32, units, first)
+    units, first = plan_units([65536] * 4, 128, 148)
+    assert set(units[:, 2].tolist()) == {18}
+    _check_plan([65536] * 4, units, first)
+
+
+def test_plan_units_on_ragged_batches():
+    import numpy as np
+    from triton_mla.kernel import plan_units
+    rng = np.random.default_rng(0)
+    for trial in range(20):
+        lens = rng.integers(0, 16385, size=int(rng.integers(1, 300))).tolist()
+        units, first = plan_units(lens, 128 if trial % 2 else 256, 148)
+        _check_plan(lens, units, first)
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(1, 16385, (256,), generator=g).tolist()
+    units, first = plan_units(lens, 128, 148)
+    _check_plan(lens, units, first)
+    lens = [65536] + [100] * 300  # one long request among many short ones is split, the short ones not
+    units, first = plan_units(lens, 128, 148)
+    _check_plan(lens, units, first)
+    assert units[units[:, 0] == 0][0, 2] > 1 and set(units[units[:, 0] > 0][:, 2].tolist()) == {1}
+
+
+def test_plan_units_edge_cases():
+    import numpy as np
+    from triton_mla.kernel import plan_units
+    units, first = plan_units([], 128, 148)
+    assert units.shape == (0, 4) and first.tolist() == [0]
+    units, first = plan_units([0, 0, 0], 128, 148)
+    assert units[:, 2].tolist() == [1, 1, 1] and first.tolist() == [0, 0, 0, 0]
+    lib = _lib.load()
+    bad = np.zeros(4, dtype=np.int32)
+    assert lib.tmla_plan_units(None, 2, 128, 148, 8, bad.ctypes.data, bad.ctypes.data) < 0

@@ -340,3 +340,86 @@ def test_kernel_selection_for_deepseek_shape(device):
     bt3 = torch.zeros(2, 4, dtype=torch.int32, device=device)
     assert selected_kernel(q[:2], kv3, bt3) == "generic"
     assert selected_kernel(q[:2].float(), kv3.float(), bt3) == "generic"
+
+
+# ----------------------------------------------------------------------------- per-request split plans
+# num_splits=None on a ragged batch runs the planner's per-request split counts, units
+# longest first (tmla_decode_units), with the merge over per-request slot ranges.
+@pytest.mark.parametrize("lens,num_heads,page_size,dtype", [
+    ([4096, 1000, 0, 65, 3000, 64, 1, 7777], 128, 64, torch.bfloat16),
+    ([300, 0, 0, 12000, 5], 20, 16, torch.bfloat16),
+    ([2048, 100, 5000, 1, 64, 9000], 129, 64, torch.float16),
+    ([65536, 100, 200, 0, 37], 128, 64, torch.bfloat16),
+])
+def test_ragged_split_plan_matches_reference(device, lens, num_heads, page_size, dtype):
+    from triton_mla.kernel import plan_units
+    units, _ = plan_units(lens, num_heads)
+    case = recipes.paged_case(lens, num_heads, page_size, seed=21, dtype=dtype)
+    out, lse = run(case, device)
+    ref_out, ref_lse = oracle_of(case)
+    check(out, lse, ref_out, ref_lse, lens)
+    assert read_status(device) == 0
+    if lens[0] == 65536:
+        assert units[units[:, 0] == 0][0, 2] > 1, "the long request is split"
+
+
+def test_ragged_split_plan_dense_cache_and_agreement(device):
+    g = torch.Generator().manual_seed(5)
+    B, S = 5, 3000
+    q = torch.randn(B, 128, 576, generator=g).to(torch.bfloat16)
+    kv = torch.randn(B, S, 576, generator=g).to(torch.bfloat16)
+    lens = torch.tensor([3000, 17, 0, 2048, 999], dtype=torch.int32)
+    case = dict(q=q, kv=kv, seqlens=lens, block_table=None, scale=recipes.SCALE_192)
+    c = to_dev(case, device)
+    out_p, lse_p = mla_decode(c["q"], c["kv"], c["seqlens"], None, softmax_scale=c["scale"], return_lse=True)
+    out_u, lse_u = mla_decode(c["q"], c["kv"], c["seqlens"], None, softmax_scale=c["scale"], return_lse=True,
+                              num_splits=3)
+    ref_out, ref_lse = oracle_of(case)
+    check(out_p, lse_p, ref_out, ref_lse, lens.tolist())
+    assert (out_p.float() - out_u.float()).abs().max().item() <= OUT_TOL
+
+
+def test_ragged_split_plan_many_short_requests(device):
+    """A long request among many empty and one-tile ones."""
+    lens = [60000] + [0] * 400 + [37] * 1200
+    case = recipes.paged_case(lens, 128, 64, seed=8)
+    out, lse = run(case, device)
+    sel = [0, 1, 400, 401, 1000, 1600]
+    sub = dict(q=case["q"][sel], kv=case["kv"], seqlens=case["seqlens"][sel], block_table=case["block_table"][sel],
+               scale=case["scale"])
+    ref_out, ref_lse = oracle_of(sub)
+    check(out[sel], lse[sel], ref_out, ref_lse, [lens[i] for i in sel])
+    assert read_status(device) == 0
+
+
+def test_split_plan_reused_across_lengths_and_in_a_graph(device):
+    """A SplitPlan says how many splits each request gets, not where they start, so it stays
+    valid when the lengths change, eagerly and inside a captured CUDA graph."""
+    from triton_mla import make_split_plan
+    lens0 = [4096, 100, 0, 7000, 33]
+    case = recipes.paged_case(lens0, 128, 64, seed=3)
+    c = to_dev(case, device)
+    plan = make_split_plan(c["seqlens"], 128)
+    assert plan.num_slots > 0, "the long requests are split"
+    lens = c["seqlens"].clone()
+    q = c["q"].clone()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        mla_decode(q, c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True, plan=plan)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        g_out, g_lse = mla_decode(q, c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True,
+                                  plan=plan)
+    for new in (lens0, [10, 4000, 300, 1, 7040], [7040, 0, 7040, 64, 65]):
+        lens.copy_(torch.tensor(new, dtype=torch.int32, device=device))
+        e_out, e_lse = mla_decode(q, c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True,
+                                  plan=plan)
+        graph.replay()
+        torch.cuda.synchronize(device)
+        sub = dict(case, seqlens=torch.tensor(new, dtype=torch.int32))
+        ref_out, ref_lse = oracle_of(sub)
+        check(e_out, e_lse, ref_out, ref_lse, new)
+        check(g_out, g_lse, ref_out, ref_lse, new)
+    del graph

@@ -10,6 +10,11 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <algorithm>
+#include <functional>
+#include <queue>
+#include <vector>
+
 #include "tmla_common.cuh"
 
 namespace tmla {
@@ -17,7 +22,10 @@ int launch_generic(const TmlaDecodeParams& p, cudaStream_t stream);
 int launch_combine(const float* ws_o, const float* ws_lse, void* out, int64_t osb, int64_t osh, float* lse,
                    int64_t lsb, int B, int H, int S, int DV, int dtype, cudaStream_t stream);
 int sm100_supported(const TmlaDecodeParams& p);
-int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream);
+int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* units = nullptr,
+                 int32_t num_units = 0, int32_t num_slots = 0);
+int launch_combine_slots(const float* ws_o, const float* ws_lse, const int32_t* req_first, void* out, int64_t osb,
+                         int64_t osh, float* lse, int64_t lsb, int B, int H, int DV, int dtype, cudaStream_t stream);
 }  // namespace tmla
 
 namespace {
@@ -168,4 +176,123 @@ int tmla_decode(const TmlaDecodeParams* p, void* stream) {
                       p->batch, p->num_heads, p->num_splits, p->d_v, p->dtype, stream);
 }
 
+// ---------------------------------------------------------------- per-request split plan
+// Costs in units of "one 2-CTA cluster streaming one 64-token tile": a work unit costs its
+// tiles plus a fixed start-up / epilogue cost, plus the write and read-back of its fp32
+// partial when its request is split.
+namespace {
+constexpr double kUnitFixedTiles = 8.0;
+constexpr double kUnitMergeTiles = 2.0;
+constexpr int kMaxSplitsPerRequest = 64;
+
+double lpt_makespan(std::vector<double>& costs, int machines) {
+  std::sort(costs.begin(), costs.end(), std::greater<double>());
+  std::priority_queue<double, std::vector<double>, std::greater<double>> load;
+  for (int i = 0; i < machines; ++i) load.push(0.0);
+  double span = 0.0;
+  for (double c : costs) {
+    double l = load.top() + c;
+    load.pop();
+    load.push(l);
+    span = std::max(span, l);
+  }
+  return span;
+}
+}  // namespace
+
+int32_t tmla_plan_units(const int32_t* seqlens, int32_t batch, int32_t num_heads, int32_t num_sms, int32_t max_units,
+                        int32_t* units, int32_t* req_first) {
+  if (!seqlens || batch < 0 || num_heads <= 0 || max_units < 0 || !req_first || (batch > 0 && !units))
+    return -TMLA_ERR_INVALID_ARG;
+  req_first[0] = 0;
+  if (batch == 0) return 0;
+  if (num_sms <= 0) num_sms = 148;
+  const int head_tiles = (num_heads + 127) / 128;
+  const int machines = std::max(1, num_sms / 2 / head_tiles);  // units running at once
+  std::vector<int> tiles(batch);
+  int max_tiles = 0;
+  for (int b = 0; b < batch; ++b) {
+    tiles[b] = seqlens[b] > 0 ? (seqlens[b] + 63) / 64 : 0;
+    max_tiles = std::max(max_tiles, tiles[b]);
+  }
+  // Candidate targets: the longest request cut into k equal parts, k = 1 .. 64.
+  int best_target = std::max(1, max_tiles);
+  double best_span = INFINITY;
+  long best_units = 0;
+  std::vector<double> costs;
+  for (int k = 1; k <= kMaxSplitsPerRequest; ++k) {
+    const int target = std::max(1, (max_tiles + k - 1) / k);
+    if (k > 1 && target == (max_tiles + k - 2) / (k - 1)) continue;  // same target as k - 1
+    costs.clear();
+    long n = 0;
+    for (int b = 0; b < batch; ++b) {
+      const int ns = std::min(kMaxSplitsPerRequest, std::max(1, (tiles[b] + target - 1) / target));
+      const int per = (tiles[b] + ns - 1) / ns;
+      for (int s = 0; s < ns; ++s) costs.push_back(per + kUnitFixedTiles + (ns > 1 ? kUnitMergeTiles : 0.0));
+      n += ns;
+    }
+    if (n > max_units) continue;
+    const double span = lpt_makespan(costs, machines);
+    if (span < best_span * (1.0 - 1e-9) || (span <= best_span * (1.0 + 1e-9) && n < best_units)) {
+      best_span = span;
+      best_target = target;
+      best_units = n;
+    }
+  }
+  if (best_units == 0) return -TMLA_ERR_INVALID_ARG;  // max_units too small for one unit per request
+  // Emit the plan: slots per request in request order, units longest first.
+  struct Unit {
+    int b, split, ns, slot, per;
+  };
+  std::vector<Unit> plan;
+  plan.reserve(best_units);
+  int slot = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int ns = std::min(kMaxSplitsPerRequest, std::max(1, (tiles[b] + best_target - 1) / best_target));
+    const int per = (tiles[b] + ns - 1) / ns;
+    for (int s = 0; s < ns; ++s) {
+      const int first_tile = std::min(tiles[b], s * per);
+      const int mine = std::min(tiles[b], first_tile + per) - first_tile;
+      plan.push_back({b, s, ns, ns > 1 ? slot + s : -1, mine});
+    }
+    if (ns > 1) slot += ns;
+    req_first[b + 1] = slot;
+  }
+  std::stable_sort(plan.begin(), plan.end(), [](const Unit& a, const Unit& c) { return a.per > c.per; });
+  for (size_t u = 0; u < plan.size(); ++u) {
+    units[4 * u] = plan[u].b;
+    units[4 * u + 1] = plan[u].split;
+    units[4 * u + 2] = plan[u].ns;
+    units[4 * u + 3] = plan[u].slot;
+  }
+  return (int32_t)plan.size();
+}
+
+size_t tmla_units_workspace_bytes(int32_t num_slots, int32_t num_heads, int32_t d_v) {
+  if (num_slots <= 0 || num_heads <= 0 || d_v <= 0) return 0;
+  const size_t o = (((size_t)num_slots * num_heads * d_v * sizeof(float)) + 255) & ~(size_t)255;
+  const size_t l = (((size_t)num_slots * num_heads * sizeof(float)) + 255) & ~(size_t)255;
+  return o + l;
+}
+
+int tmla_decode_units(const TmlaDecodeParams* p, const int32_t* units, const int32_t* req_first, int32_t num_units,
+                      int32_t num_slots, void* stream) {
+  if (!p) return TMLA_ERR_INVALID_ARG;
+  TmlaDecodeParams q = *p;
+  q.num_splits = 1;
+  q.flags &= ~TMLA_FLAG_PARTIAL_ONLY;
+  int rc = validate(&q);
+  if (rc) return rc;
+  if (q.batch == 0) return TMLA_OK;
+  if (!units || !req_first || num_units < q.batch || num_units > 65535 || num_slots < 0) return TMLA_ERR_INVALID_ARG;
+  if (num_slots > 0 && (!q.ws_o || !q.ws_lse)) return TMLA_ERR_WORKSPACE;
+  if (q.kernel == TMLA_KERNEL_GENERIC || !tmla::sm100_supported(q)) return TMLA_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = finish(tmla::launch_sm100(q, s, units, num_units, num_slots));
+  if (rc || num_slots == 0) return rc;
+  return finish(tmla::launch_combine_slots(q.ws_o, q.ws_lse, req_first, q.out, q.out_stride_b, q.out_stride_h, q.lse,
+                                           q.lse_stride_b, q.batch, q.num_heads, q.d_v, q.dtype, s));
+}
+
 }  // extern "C"
+

@@ -106,6 +106,64 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
   if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
 }
 
+// Merge of a per-request split plan (tmla_decode_units): request b's partials sit in slots
+// req_first[b] .. req_first[b + 1] - 1 of ws_o [slots, H, DV] / ws_lse [slots, H]; a request
+// with no slots (one split) was written by the split kernel and is skipped.  Same layout of
+// the work and the same arithmetic as mla_combine_vec_kernel.
+template <typename T>
+__global__ void __launch_bounds__(kCombineWarps * 32)
+    mla_combine_slots_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
+                             const int32_t* __restrict__ req_first, T* __restrict__ out, int64_t osb, int64_t osh,
+                             float* __restrict__ lse, int64_t lsb, int B, int H, int DV) {
+  ptx::griddep_wait();
+  const int lane = threadIdx.x & 31;
+  const int groups = DV / 128;
+  const int64_t wid = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
+  if (wid >= (int64_t)B * H * groups) return;
+  const int64_t row = wid / groups;
+  const int grp = (int)(wid - row * groups);
+  const int b = (int)(row / H), h = (int)(row - (int64_t)b * H);
+  const int s0 = req_first[b], S = req_first[b + 1] - s0;
+  if (S <= 0) return;
+  const float4* src = reinterpret_cast<const float4*>(ws_o + ((int64_t)s0 * H + h) * DV + grp * 128) + lane;
+  const int64_t sstride = (int64_t)H * DV / 4;
+  float4 v[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) v[u] = (u < S) ? __ldg(src + u * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* L = ws_lse + (int64_t)s0 * H + h;
+  const float l0 = lane < S ? L[(int64_t)lane * H] : -INFINITY;
+  const float l1 = lane + 32 < S ? L[(int64_t)(lane + 32) * H] : -INFINITY;
+  float m = fmaxf(l0, l1);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (m == -INFINITY) m = 0.f;
+  const float w0 = exp2f(l0 - m), w1 = exp2f(l1 - m);
+  float wsum = w0 + w1;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int q0 = 0; q0 < S; q0 += 8) {
+    float w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int sp = q0 + u;
+      w[u] = __shfl_sync(0xffffffffu, sp < 32 ? w0 : w1, sp & 31);
+      if (q0 > 0) v[u] = (sp < S) ? __ldg(src + sp * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc.x = fmaf(w[u], v[u].x, acc.x);
+      acc.y = fmaf(w[u], v[u].y, acc.y);
+      acc.z = fmaf(w[u], v[u].z, acc.z);
+      acc.w = fmaf(w[u], v[u].w, acc.w);
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
+  T* dst = out + (int64_t)b * osb + (int64_t)h * osh + grp * 128 + 4 * lane;
+  store4<T>(dst, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+  if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+}
+
 // General path (any d_v, any split count): one warp per row, serial over splits.
 template <typename T>
 __global__ void __launch_bounds__(kCombineWarps * 32)
@@ -167,6 +225,42 @@ static int launch_combine_t(const float* ws_o, const float* ws_lse, void* out, i
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
+}
+
+template <typename T>
+static int launch_combine_slots_t(const float* ws_o, const float* ws_lse, const int32_t* req_first, void* out,
+                                  int64_t osb, int64_t osh, float* lse, int64_t lsb, int B, int H, int DV,
+                                  cudaStream_t stream) {
+  const int64_t warps = (int64_t)B * H * (DV / 128);
+  if (warps == 0) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(kCombineWarps * 32);
+  cfg.gridDim = dim3((unsigned)((warps + kCombineWarps - 1) / kCombineWarps));
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, mla_combine_slots_kernel<T>, ws_o, ws_lse, req_first, static_cast<T*>(out),
+                                     osb, osh, lse, lsb, B, H, DV);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -(int)e;
+}
+
+// Merge of a per-request split plan; d_v a multiple of 128, at most 64 splits per request
+// (the planner's limit), 16-byte aligned out rows.
+int launch_combine_slots(const float* ws_o, const float* ws_lse, const int32_t* req_first, void* out, int64_t osb,
+                         int64_t osh, float* lse, int64_t lsb, int B, int H, int DV, int dtype, cudaStream_t stream) {
+  if (DV % 128) return TMLA_ERR_UNSUPPORTED;
+  switch (dtype) {
+    case TMLA_DTYPE_BF16:
+      return launch_combine_slots_t<__nv_bfloat16>(ws_o, ws_lse, req_first, out, osb, osh, lse, lsb, B, H, DV, stream);
+    case TMLA_DTYPE_FP16:
+      return launch_combine_slots_t<__half>(ws_o, ws_lse, req_first, out, osb, osh, lse, lsb, B, H, DV, stream);
+    default:
+      return TMLA_ERR_UNSUPPORTED;
+  }
 }
 
 int launch_combine(const float* ws_o, const float* ws_lse, void* out, int64_t osb, int64_t osh, float* lse,

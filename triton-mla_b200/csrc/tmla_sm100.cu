@@ -67,6 +67,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include "tmla_common.cuh"
 #include "tmla_ptx.cuh"
 
@@ -239,6 +241,9 @@ struct KernelArgs {
   TmlaDecodeParams p;
   int rows_per_load;   // g: token rows per TMA box (64 for dense / page % 64 == 0)
   float scale_log2;    // softmax_scale * log2(e)
+  // Per-request split plan (tmla_decode_units) or NULL: entry z = {request, split,
+  // splits of that request, partial slot (-1: the request has one split)}.
+  const int4* units;
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool fp16) {
@@ -338,7 +343,8 @@ __device__ __forceinline__ void stage_rows(unsigned char* tiles, uint32_t t_row,
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_sm100_split_kernel(const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
-                           const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_q_rope,
+                           const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_part,
+                           const __grid_constant__ CUtensorMap tm_q_rope,
                            const __grid_constant__ KernelArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const TmlaDecodeParams& p = args.p;
@@ -356,7 +362,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t peer = rank ^ 1u;
   const int head_tile = blockIdx.x >> 1;
   const int h0 = head_tile * 128;
-  const int split = blockIdx.y, b = blockIdx.z;
+  // Which split of which request: the grid's (y, z) for uniform splits, or a plan entry.
+  int split = blockIdx.y, b = blockIdx.z, nsplit = p.num_splits, slot = -1;
+  if (args.units) {
+    const int4 un = __ldg(args.units + blockIdx.z);
+    b = un.x, split = un.y, nsplit = un.z, slot = un.w;
+  }
+  // One split writes the final output (and natural-log LSE); several write fp32 partials.
+  const bool final_out = args.units ? nsplit == 1 : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
   const int H = p.num_heads;
   Waiter waiter{abort_flag, p.status};
 #ifdef TMLA_TRACE_ENABLED
@@ -377,7 +390,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   int spec_start = 0, pg_spec = 0;
   if (warp == kWarpProducer) {
     int spec_end;
-    split_range(cap, p.num_splits, split, spec_start, spec_end);
+    split_range(cap, nsplit, split, spec_start, spec_end);
     const int t = spec_start + lane * g;
     if (lane < nsub && t < spec_end) pg_spec = p.block_table ? __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size) : b;
   }
@@ -441,7 +454,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == kWarpProducer && lane == 0) {
     prefetch_tmap(&tm_kv_lat);
     prefetch_tmap(&tm_kv_rope);
-    prefetch_tmap(&tm_out);
     prefetch_tmap(&tm_q_rope);
   }
 
@@ -452,7 +464,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     len = len < 0 ? 0 : cap;
   }
   int start, end;
-  split_range(len, p.num_splits, split, start, end);
+  split_range(len, nsplit, split, start, end);
   const int ntiles = end > start ? (end - start + kTile - 1) / kTile : 0;
 
   // ------------------------------------------------------------ TMA producer, part 1
@@ -892,10 +904,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           lstat[2 * row] = l;
           const int hh = h0 + row;
           if (hh < H) {
-            const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
             const float lse2 = l > 0.f ? mf + log2f(l) : -INFINITY;
             if (final_out) {
               if (p.lse) p.lse[(int64_t)b * p.lse_stride_b + hh] = l > 0.f ? lse2 * kLn2 : -INFINITY;
+            } else if (args.units) {
+              p.ws_lse[(int64_t)slot * H + hh] = lse2;
             } else {
               p.ws_lse[((int64_t)b * H + hh) * p.num_splits + split] = lse2;
             }
@@ -920,7 +933,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (wg == 0 && quarter == 0 && lane == 0) TMLA_SPAN(5);
       const float l = lstat[2 * (quarter * 32 + lane)];
-      const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
       stage_rows<T>(smem_gen + kOffStages, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
                     4 * wg, 4, final_out);
       fence_proxy_async_smem();
@@ -934,10 +946,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < 4; ++c)
               tma_store_3d(&tm_out, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 64 * c, h0, b);
+          } else if (args.units) {
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c)
+              tma_store_3d(&tm_part, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 32 * c, h0,
+                           slot);
           } else {
 #pragma unroll 1
             for (int c = 0; c < 8; ++c)
-              tma_store_4d(&tm_out, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 32 * c, split,
+              tma_store_4d(&tm_part, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 32 * c, split,
                            h0, b);
           }
           bulk_commit_group();
@@ -1027,6 +1044,21 @@ static int encode_partials(CUtensorMap* map, float* ws_o, int batch, int heads, 
   return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
 }
 
+// The fp32 partials of a per-request split plan, ws_o [slots, heads, 512], as a 3-D map with
+// boxes of 32 columns x 128 heads x 1 slot.
+static int encode_slot_partials(CUtensorMap* map, float* ws_o, int slots, int heads) {
+  auto fn = encode_fn();
+  if (!fn) return TMLA_ERR_CUDA;
+  cuuint64_t dims[3] = {512, (cuuint64_t)heads, (cuuint64_t)slots};
+  cuuint64_t strides[2] = {512 * 4, (cuuint64_t)heads * 512 * 4};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ws_o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
+}
+
+// Token rows per TMA box: the largest power of two <= kTile dividing the page size.
 static int pow2_rows(int page) {
   int g = 64;
   while (g > 1 && page % g) g >>= 1;
@@ -1046,14 +1078,17 @@ int sm100_supported(const TmlaDecodeParams& p) {
   return 1;
 }
 
-int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
+int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* units, int32_t num_units,
+                 int32_t num_slots) {
   using namespace sm100;
   if (!sm100_supported(p)) return TMLA_ERR_UNSUPPORTED;
   const CUtensorMapDataType dt =
       p.dtype == TMLA_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int g = p.block_table ? pow2_rows(p.page_size) : kTile;
   const uint64_t pages = p.block_table ? (uint64_t)p.num_pages : (uint64_t)p.batch;
-  CUtensorMap tm_lat, tm_rope, tm_q, tm_out;
+  CUtensorMap tm_lat, tm_rope, tm_q, tm_out, tm_part;
+  memset(&tm_out, 0, sizeof(tm_out));
+  memset(&tm_part, 0, sizeof(tm_part));
   int rc = encode3d(&tm_lat, dt, p.kv, 576, (uint64_t)p.page_size, pages, (uint64_t)p.kv_stride_tok * 2,
                     (uint64_t)p.kv_stride_page * 2, 64, (uint32_t)g, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc)
@@ -1062,27 +1097,34 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream) {
   if (!rc)
     rc = encode3d(&tm_q, dt, p.q, 576, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.q_stride_h * 2,
                   (uint64_t)p.q_stride_b * 2, kHalfRope, 128, CU_TENSOR_MAP_SWIZZLE_64B);
-  const bool final_out = (p.num_splits == 1) && !(p.flags & TMLA_FLAG_PARTIAL_ONLY);
-  if (!rc && final_out)
+  // The final 16-bit output (one split) and the fp32 partials (several) as tensor maps;
+  // a plan of per-request splits can need both in one launch.
+  const bool any_final = units ? num_slots < num_units : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
+  const bool any_part = units ? num_slots > 0 : !any_final;
+  if (!rc && any_final)
     rc = encode3d(&tm_out, dt, p.out, 512, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.out_stride_h * 2,
                   (uint64_t)p.out_stride_b * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc && !final_out) rc = encode_partials(&tm_out, p.ws_o, p.batch, p.num_heads, p.num_splits);
+  if (!rc && any_part) {
+    rc = units ? encode_slot_partials(&tm_part, p.ws_o, num_slots, p.num_heads)
+               : encode_partials(&tm_part, p.ws_o, p.batch, p.num_heads, p.num_splits);
+  }
   if (rc) return rc;
   KernelArgs a;
   a.p = p;
   a.rows_per_load = g;
   a.scale_log2 = p.softmax_scale * kLog2e;
-  const dim3 grid(2 * ((p.num_heads + 127) / 128), p.num_splits, p.batch);
+  a.units = reinterpret_cast<const int4*>(units);
+  const dim3 grid(2 * ((p.num_heads + 127) / 128), units ? 1 : p.num_splits, units ? num_units : p.batch);
   cudaError_t e;
   if (p.dtype == TMLA_DTYPE_FP16) {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      mla_sm100_split_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_q, a);
+      mla_sm100_split_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
   } else {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
     if (e == cudaSuccess)
-      mla_sm100_split_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_q, a);
+      mla_sm100_split_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;

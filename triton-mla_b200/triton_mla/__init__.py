@@ -6,7 +6,7 @@ Exports the same names as the reference package (src/triton_mla/__init__.py:1-14
 """
 
 from . import layer_ops, sharding
-from .kernel import get_num_splits, mla_decode, read_status, selected_kernel
+from .kernel import SplitPlan, get_num_splits, make_split_plan, mla_decode, read_status, selected_kernel
 from .model import MLA, MLAConfig, MLADecodeGraph
 from .reference import mla_decode_ref, mla_decode_torch
 
@@ -16,7 +16,9 @@ __all__ = [
     "MLA",
     "MLAConfig",
     "MLADecodeGraph",
+    "SplitPlan",
     "get_num_splits",
+    "make_split_plan",
     "mla_decode",
     "mla_decode_ref",
     "mla_decode_torch",

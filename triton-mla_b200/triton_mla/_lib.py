@@ -55,6 +55,9 @@ EXPORTED = (
     "tmla_q_absorb_rope",
     "tmla_kv_norm_rope_append",
     "tmla_o_unabsorb",
+    "tmla_plan_units",
+    "tmla_units_workspace_bytes",
+    "tmla_decode_units",
 )
 
 
@@ -212,6 +215,12 @@ def load() -> ctypes.CDLL:
     lib.tmla_abi_version.restype = ctypes.c_int
     lib.tmla_params_bytes.argtypes = []
     lib.tmla_params_bytes.restype = ctypes.c_size_t
+    lib.tmla_plan_units.argtypes = [vp, i32, i32, i32, i32, vp, vp]
+    lib.tmla_plan_units.restype = i32
+    lib.tmla_units_workspace_bytes.argtypes = [i32, i32, i32]
+    lib.tmla_units_workspace_bytes.restype = ctypes.c_size_t
+    lib.tmla_decode_units.argtypes = [P, vp, vp, i32, i32, vp]
+    lib.tmla_decode_units.restype = ctypes.c_int
     for name, st in (("tmla_q_absorb_rope", TmlaQPrepParams), ("tmla_kv_norm_rope_append", TmlaKvAppendParams),
                      ("tmla_o_unabsorb", TmlaOUnabsorbParams)):
         fn = getattr(lib, name)

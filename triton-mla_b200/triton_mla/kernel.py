@@ -47,6 +47,60 @@ def _num_sms(device) -> int:
     return B200_NUM_SMS
 
 
+def plan_units(seqlens, num_heads: int, num_sms: int = B200_NUM_SMS):
+    """Per-request split plan for a batch (``tmla_plan_units``; host only, no GPU).
+
+    Returns ``(units, req_first)`` as int32 numpy arrays: ``units[u] = (request, split,
+    splits of that request, partial slot or -1)``, longest unit first, and
+    ``req_first[b]`` the first partial slot of request b (``req_first[-1]`` slots in all).
+    """
+    import numpy as np
+
+    lens = np.ascontiguousarray(np.asarray(seqlens, dtype=np.int32).reshape(-1))
+    batch = lens.shape[0]
+    cap = max(1, batch * 64)
+    units = np.zeros((cap, 4), dtype=np.int32)
+    req_first = np.zeros(batch + 1, dtype=np.int32)
+    n = _lib.load().tmla_plan_units(lens.ctypes.data, batch, int(num_heads), int(num_sms), cap, units.ctypes.data,
+                                    req_first.ctypes.data)
+    if n < 0:
+        raise _lib.LibraryError(-n, "tmla_plan_units")
+    return units[:n].copy(), req_first
+
+
+class SplitPlan:
+    """A per-request split plan in device memory, for ``mla_decode(..., plan=...)``.
+
+    It says how many splits each request gets and in which order the work units run, not
+    where the splits start: the kernels cut each request's tokens from its length on the
+    device.  So a plan stays valid when the lengths change (a decode loop can plan once per
+    batch composition) and a call with a plan needs no host sync (CUDA-graph safe).
+    """
+
+    def __init__(self, units, req_first, device):
+        self.batch = int(req_first.shape[0]) - 1
+        self.num_units = int(units.shape[0])
+        self.num_slots = int(req_first[-1])
+        self.units = torch.from_numpy(units).to(device)
+        self.req_first = torch.from_numpy(req_first).to(device)
+        self.splits = units[:, 2].copy()  # per unit, on the host
+
+
+def make_split_plan(cache_seqlens, num_heads: int, device=None) -> SplitPlan:
+    """Plan per-request splits for the lengths ``cache_seqlens`` (a tensor or a sequence) with
+    ``tmla_plan_units`` on the host, and put the plan on ``device``."""
+    import numpy as np
+
+    if isinstance(cache_seqlens, torch.Tensor):
+        device = cache_seqlens.device if device is None else device
+        lens = cache_seqlens.detach().to("cpu", torch.int32).numpy()
+    else:
+        lens = np.asarray(cache_seqlens, dtype=np.int32)
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    units, req_first = plan_units(lens, num_heads, _num_sms(device))
+    return SplitPlan(units, req_first, device)
+
+
 def get_num_splits(batch, num_heads, max_seqlen, num_sms, min_tokens_per_split=128):
     """Split count for one decode call on B200.
 
@@ -118,6 +172,7 @@ def mla_decode(
     *,
     kernel: str = "auto",
     out: torch.Tensor = None,
+    plan: "SplitPlan" = None,
 ):
     """Weight-absorbed MLA decode attention over a shared latent KV cache.
 
@@ -133,6 +188,8 @@ def mla_decode(
         num_splits: KV splits; None picks one (one host sync); pass it
             explicitly for CUDA-graph capture.
         return_lse: also return the natural-log log-sum-exp per head.
+        plan: keyword-only, a ``SplitPlan`` (``make_split_plan``) to follow instead of
+            ``num_splits``: per-request split counts, no host sync (tcgen05 kernel only).
         kernel: keyword-only, "auto" (tcgen05 kernel where the shape allows),
             "sm100" (require it) or "generic" (CUDA-core kernel).
         out: keyword-only preallocated [batch, num_heads, head_dim_v] output.
@@ -182,13 +239,32 @@ def mla_decode(
         bt_stride = 0
 
     device = q.device
-    if num_splits is None:
+    if plan is not None:
+        assert plan.batch == batch, "the split plan was made for another batch size"
+        num_splits = 1
+    elif num_splits is None:
         if batch > 0 and torch.cuda.is_current_stream_capturing():
             # No host sync during capture: size the splits for the longest request the cache holds.
             max_seqlen = bt_width * page_size if paged else kv_cache.shape[1]
+            num_splits = get_num_splits(batch, num_heads, max_seqlen, _num_sms(device))
+        elif batch > 0:
+            # The one host sync (the reference reads max(cache_seqlens) here, kernel.py:264-266).
+            lens_host = cache_seqlens.cpu()
+            if kernel != "generic" and selected_kernel(q, kv_cache, block_table, head_dim_v, num_splits=1,
+                                                       kernel=kernel) == "sm100":
+                # The tcgen05 kernel takes a split count per request: the planner's choice.
+                units, req_first = plan_units(lens_host.numpy(), num_heads, _num_sms(device))
+                counts = units[:, 2]
+                tiles = (lens_host + 63) // 64
+                if counts.min() == counts.max() and int(tiles.min()) == int(tiles.max()):
+                    num_splits = int(counts[0])  # equal requests split the same way: the uniform grid
+                else:
+                    plan = SplitPlan(units, req_first, device)
+                    num_splits = 1
+            if num_splits is None:
+                num_splits = get_num_splits(batch, num_heads, int(lens_host.max()), _num_sms(device))
         else:
-            max_seqlen = int(cache_seqlens.max().item()) if batch > 0 else 0
-        num_splits = get_num_splits(batch, num_heads, max_seqlen, _num_sms(device))
+            num_splits = 1
     num_splits = int(num_splits)
 
     if out is None:
@@ -200,11 +276,16 @@ def mla_decode(
         return (out, lse) if return_lse else out
 
     lib = _lib.load()
-    ws_bytes = lib.tmla_workspace_bytes(batch, num_heads, num_splits, head_dim_v)
+    if plan is not None:
+        slots = plan.num_slots
+        ws_bytes = lib.tmla_units_workspace_bytes(slots, num_heads, head_dim_v)
+        o_bytes = (slots * num_heads * head_dim_v * 4 + 255) & ~255
+    else:
+        ws_bytes = lib.tmla_workspace_bytes(batch, num_heads, num_splits, head_dim_v)
+        o_bytes = (batch * num_heads * num_splits * head_dim_v * 4 + 255) & ~255
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
     ws_o = ws_lse = None
     if ws is not None:
-        o_bytes = (batch * num_heads * num_splits * head_dim_v * 4 + 255) & ~255
         ws_o = ws.data_ptr()
         ws_lse = ws_o + o_bytes
 
@@ -223,7 +304,12 @@ def mla_decode(
         torch.cuda.set_device(device)
     try:
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.tmla_decode(ctypes.byref(p), ctypes.c_void_p(stream)), "tmla_decode")
+        if plan is None:
+            _lib.check(lib.tmla_decode(ctypes.byref(p), ctypes.c_void_p(stream)), "tmla_decode")
+        else:
+            _lib.check(lib.tmla_decode_units(ctypes.byref(p), plan.units.data_ptr(), plan.req_first.data_ptr(),
+                                             plan.num_units, plan.num_slots, ctypes.c_void_p(stream)),
+                       "tmla_decode_units")
     finally:
         if prev != device.index:
             torch.cuda.set_device(prev)
