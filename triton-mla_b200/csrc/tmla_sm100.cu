@@ -111,8 +111,10 @@ using namespace ptx;
 constexpr int kTile = 64;                 // tokens per pipeline stage
 constexpr int kStages = 4;                // latent cache-tile ring depth (held until PV)
 constexpr int kRopeSlots = 2;             // RoPE cache-tile ring depth (held until QK)
-constexpr int kSinBufs = 2;               // score-exchange buffers
-static_assert(kSinBufs == 2, "one score-exchange buffer per softmax warpgroup");
+constexpr int kSinBufs = 2;               // score-exchange buffers (1 or 2)
+constexpr int kPBufs = 2;                 // P buffers, the A operand of PV (1 or 2)
+static_assert(kSinBufs == 1 || kSinBufs == 2, "score-exchange buffers");
+static_assert(kPBufs == 1 || kPBufs == 2, "P buffers");
 constexpr int kThreads = 512;
 constexpr int kHalfLatent = 256;          // latent columns per CTA
 constexpr int kHalfRope = 32;             // RoPE columns per CTA
@@ -132,7 +134,7 @@ constexpr uint32_t kStatBytes = 128 * 8;  // final (l, m) of all 128 rows for th
 constexpr uint32_t kOffStages = 0;
 constexpr uint32_t kOffRope = kOffStages + kStages * kStageBytes;
 constexpr uint32_t kOffPBuf = kOffRope + kRopeSlots * kRopeBytes;  // P buffers: A operand of PV (1024-aligned)
-constexpr uint32_t kOffQRope = kOffPBuf + 2 * kPBufBytes;
+constexpr uint32_t kOffQRope = kOffPBuf + kPBufs * kPBufBytes;
 constexpr uint32_t kOffSin = kOffQRope + kQRopeBytes;
 constexpr uint32_t kOffAlpha = kOffSin + kSinBufs * kSinBytes;  // alpha is double-buffered
 constexpr uint32_t kOffMx = kOffAlpha + 2 * kAlphaBytes;      // running maxima handed between the warpgroups
@@ -604,7 +606,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         TMLA_TRACE(2, j);
         if (j == ntiles - 1) TMLA_SPAN(4);
         tc_fence_after();
-        const uint32_t st = sh.stage(j % kStages), pbuf = sh.base + kOffPBuf + pb * kPBufBytes;
+        const uint32_t st = sh.stage(j % kStages), pbuf = sh.base + kOffPBuf + (j % kPBufs) * kPBufBytes;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
           // A = P: 128 rows x 16 tokens, K-major 128B-swizzled (same layout as a Q box).
@@ -632,10 +634,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // returned data (see after_loads), so when this thread sees a phase complete
     // the peer may overwrite that buffer.
     if (lane == 0) {
+      // It also arms each Sin buffer's barrier for the bytes of its next tile, in tile
+      // order: a buffer's next phase is armed only after its last one was consumed.
       const uint32_t soutempty_remote = map_to_rank(sh.bar(kBarSoutEmpty0), peer);  // + 8 * buffer
+      for (int j = 0; j < ntiles && j < kSinBufs; ++j) mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + j), kSinBytes);
       for (int j = 0; j < ntiles; ++j) {
         const int ib = j % kSinBufs;
         if (!waiter.wait(sh.bar(kBarSinRead0 + ib), (j / kSinBufs) & 1)) break;
+        if (j + kSinBufs < ntiles) mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + ib), kSinBytes);
         mbar_arrive_cluster_relaxed(soutempty_remote + 8u * ib);
       }
     }
@@ -703,12 +709,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows L and L + 8 (partial sums)
       bool ok = true;
       for (int j = wg; j < ntiles; j += 2) {
-        const int sb = wg;  // S, Sin, P and alpha buffer of this tile (j % 2)
+        const int sb = wg;  // S, alpha and barrier set of this tile (j % 2)
+        const int ib = j % kSinBufs, pbi = j % kPBufs;  // its Sin buffer and P buffer
         const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (arm) {
-          mbar_arrive_expect_tx(sh.bar(kBarSinFull0 + sb), kSinBytes);
-          mbar_arrive_expect_tx(sh.bar(kBarPinFull0 + sb), kPPeerBytes + kAlphaBytes);
-        }
+        if (arm) mbar_arrive_expect_tx(sh.bar(kBarPinFull0 + sb), kPPeerBytes + kAlphaBytes);
         if (!waiter.wait(sh.bar(kBarSFull0 + sb), ph)) {
           ok = false;
           break;
@@ -726,7 +730,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarSEmpty0 + sb));
-        if (!waiter.wait(sh.bar(kBarSinFull0 + sb), ph, true)) {
+        // The running maximum after tile j-1, published by the other warpgroup once it has
+        // read Sin(j-1).  With one Sin buffer it is taken first: until Sin(j-1) was read,
+        // the buffer's barrier may still be in tile j-1's phase, whose parity differs from
+        // tile j's, and a parity wait would pass at once.
+        float mp_a = -INFINITY, mp_b = -INFINITY;
+        auto take_running_max = [&]() -> bool {
+          if (!waiter.wait(max_in, (uint32_t)((j - 1) >> 1) & 1u)) return false;
+          mp_a = m_other[orow];
+          mp_b = m_other[orow + 8];
+          return true;
+        };
+        if (kSinBufs == 1 && j > 0 && !take_running_max()) {
+          ok = false;
+          break;
+        }
+        if (!waiter.wait(sh.bar(kBarSinFull0 + ib), (uint32_t)(j / kSinBufs) & 1u, true)) {
           ok = false;
           break;
         }
@@ -734,7 +753,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t dep = 0;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float4 v = sin[sb * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
+          const float4 v = sin[ib * (kSinBytes / 16) + (quarter * 8 + c) * 32 + lane];
           dep ^= __float_as_uint(v.x) ^ __float_as_uint(v.y) ^ __float_as_uint(v.z) ^ __float_as_uint(v.w);
           s[4 * c] += v.x;
           s[4 * c + 1] += v.y;
@@ -745,7 +764,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // overwrite Sin.  The arrive's address depends on every loaded word, so it cannot
         // issue while a load of this warp is still in flight (a warp's loads complete for
         // all lanes at once).
-        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + sb), dep));
+        if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + ib), dep));
         TMLA_TRACE_IF(quarter == 0, 5, j);
 
         // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
@@ -771,15 +790,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2)) * args.scale_log2;
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2)) * args.scale_log2;
-        // The running maximum after tile j-1, published by the other warpgroup.
-        float mp_a = -INFINITY, mp_b = -INFINITY;
-        if (j > 0) {
-          if (!waiter.wait(max_in, (uint32_t)((j - 1) >> 1) & 1u)) {
-            ok = false;
-            break;
-          }
-          mp_a = m_other[orow];
-          mp_b = m_other[orow + 8];
+        if (kSinBufs == 2 && j > 0 && !take_running_max()) {
+          ok = false;
+          break;
         }
         float mn_a = mp_a, mn_b = mp_b, al_a = 1.f, al_b = 1.f;
         const bool need_a = mx_a > mp_a + kRescaleThreshold, need_b = mx_b > mp_b + kRescaleThreshold;
@@ -817,8 +830,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         l_a += sum_a;
         l_b += sum_b;
         TMLA_TRACE_IF(quarter == 0, 6, j);
-        // P buffer sb (in both CTAs) was last read by PV(j-2).
-        if (j >= 2 && !waiter.wait(sh.bar(kBarPairPvDone0 + sb), (uint32_t)((j - 2) >> 1) & 1u)) {
+        // P buffer pbi (in both CTAs) was last read by PV(j - kPBufs).
+        if (j >= kPBufs && !waiter.wait(sh.bar(kBarPairPvDone0 + ((j - kPBufs) & 1)), (uint32_t)((j - kPBufs) >> 1) & 1u)) {
           ok = false;
           break;
         }
@@ -826,7 +839,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           // Own rows of P into this CTA's buffer, in the 128B-swizzled K-major layout PV
           // reads (row r: 128 bytes at r * 128, 16-byte chunk c at (c ^ (r & 7)) * 16): word
           // t4 of chunk k holds this thread's tokens 8k + 2 t4 and 8k + 2 t4 + 1.
-          unsigned char* pbuf = smem_gen + kOffPBuf + sb * kPBufBytes;
+          unsigned char* pbuf = smem_gen + kOffPBuf + pbi * kPBufBytes;
           const int ra = quarter * 32 + 16 * (int)rank + L, rb = ra + 8;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
@@ -837,7 +850,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           __syncwarp();
           // The same 16 rows (2 KB, contiguous) into the peer's buffer, with the rescale factors.
           if (lane == 0) {
-            const uint32_t off = kOffPBuf + sb * kPBufBytes + (uint32_t)(quarter * 32 + 16 * (int)rank) * 128u;
+            const uint32_t off = kOffPBuf + pbi * kPBufBytes + (uint32_t)(quarter * 32 + 16 * (int)rank) * 128u;
             bulk_copy_to_cta(map_to_rank(sh.base + off, peer), sh.base + off, 2048u, pinfull_remote + 8u * sb);
           }
           if (t4 == 0)
