@@ -1,6 +1,6 @@
 """Benchmark of the B200 MLA decode path (one JSON line on stdout, rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference|cutlass-mla]
 
 A step is one ``mla_decode`` call over one batch of the workload (BASELINE
 config 2 by default: B=32 requests x 4096 cached tokens, H=128, bf16, paged
@@ -19,6 +19,8 @@ cached tokens, weights replicated on every rank).
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 numpy oracle) on the host cores on a bounded sample of the same workload.
+``--impl cutlass-mla`` times a library kernel (vLLM's CUTLASS sm100 MLA decode)
+on the same workload, one GPU, for comparison.
 """
 
 from __future__ import annotations
@@ -404,13 +406,86 @@ def run_reference(args):
     return 0
 
 
+def run_library(args):
+    """--impl cutlass-mla: a library MLA decode kernel on the same workload, for comparison.
+
+    It times vLLM's prebuilt CUTLASS sm100 MLA decode (``torch.ops._C.sm100_cutlass_mla_decode``),
+    with its own split choice, on the same inputs and with the same L2 flush and event timing as
+    this repository's arm.  It also reports the largest difference from ``mla_decode``'s output.
+    One GPU only.  This is a measurement, not part of the decode path.
+    """
+    line = {"impl": "cutlass-mla", "metric": METRIC, "n_gpus": args.gpus}
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus != 1:
+        line["unavailable"] = "the library comparison runs on one GPU"
+        print(json.dumps(line), flush=True)
+        return 0
+    cfg = CONFIGS[args.config]
+    if cfg.get("layer"):
+        line["unavailable"] = "the library comparison covers the decode configs (cfg2-cfg4)"
+        print(json.dumps(line), flush=True)
+        return 0
+    import torch
+    try:
+        from vllm import _custom_ops as vops
+    except Exception as e:  # noqa: BLE001
+        line["unavailable"] = f"vllm's CUTLASS MLA op does not import: {type(e).__name__}"
+        print(json.dumps(line), flush=True)
+        return 0
+    from triton_mla import mla_decode
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    q, kv, lens, bt = make_workload(cfg, device, seed=1000)
+    B = q.shape[0]
+    if bt.shape[1] % 2:  # the library reads 128-token tiles: an even number of 64-token pages per row
+        bt = torch.cat([bt, bt[:, :1]], dim=1).contiguous()
+    q_nope, q_pe = q[..., :D_V].contiguous(), q[..., D_V:].contiguous()
+    out = torch.empty(B, 128, D_V, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(B, 128, dtype=torch.float32, device=device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    ws = torch.empty(max(vops.sm100_cutlass_mla_get_workspace_size(int(lens.max()), B, sms, -1), 1),
+                     dtype=torch.uint8, device=device)
+
+    def step():
+        vops.sm100_cutlass_mla_decode(out, lse, q_nope, q_pe, kv, lens, bt, ws, SCALE, -1)
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        step()
+    ours = mla_decode(q, kv, lens, bt, softmax_scale=SCALE)
+    torch.cuda.synchronize()
+    diff = float((out.float() - ours.float()).abs().max())
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    total_tokens = int(lens.sum())
+    tflops = decode_flops(total_tokens, 128) / (ms * 1e-3) / 1e12
+    import vllm
+    line.update({
+        "value": tflops, "unit": "TFLOPS", "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "us_per_call": ms * 1e3, "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1)",
+        "config": {"workload": cfg["desc"], "batch": B, "tokens": total_tokens, "num_kv_splits": "library default (-1)",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "library": f"vllm {vllm.__version__} torch.ops._C.sm100_cutlass_mla_decode",
+        "max_abs_diff_vs_mla_decode": diff,
+    })
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "cutlass-mla"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "sm100", "generic"])
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (rank 0, N=1)")
     ap.add_argument("--clock-soak", type=float, default=0.6, help="seconds of untimed steps under the clock sampler")
@@ -418,6 +493,8 @@ def main(argv=None):
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "cutlass-mla":
+        return run_library(args)
 
     import torch
     import torch.distributed as dist
@@ -533,41 +610,76 @@ def main(argv=None):
     torch.cuda.synchronize()
     kern_ms = sum(a.elapsed_time(b) for a, b in zip(ks, ke)) / len(ks)
 
-    # ---- end to end through the public API from pinned host memory.
+    # ---- end to end through the public API from pinned host memory.  Each step copies its
+    # inputs host->device, decodes (after an L2 flush) and copies out and lse device->host.
+    # Steps are pipelined over three streams with two device input sets and two host output
+    # sets: step i+1's upload and step i-1's download overlap step i's decode.  The time
+    # from the first upload to the last download, over K steps, is the per-step time; the
+    # unpipelined latency of one step is reported beside it.
     q_h = q.cpu().pin_memory()
     lens_h = lens.cpu().pin_memory()
     bt_h = bt.cpu().pin_memory()
-    out_h = torch.empty(B, 128, D_V, dtype=torch.bfloat16).pin_memory()
-    lse_h = torch.empty(B, 128, dtype=torch.float32).pin_memory()
+    nbuf = 2
+    out_h = [torch.empty(B, 128, D_V, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    lse_h = [torch.empty(B, 128, dtype=torch.float32).pin_memory() for _ in range(nbuf)]
     h2d = q_h.numel() * 2 + lens_h.numel() * 4 + bt_h.numel() * 4
-    d2h = out_h.numel() * 2 + lse_h.numel() * 4
+    d2h = out_h[0].numel() * 2 + lse_h[0].numel() * 4
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    q_d = [torch.empty_like(q) for _ in range(nbuf)]
+    lens_d = [torch.empty_like(lens) for _ in range(nbuf)]
+    bt_d = [torch.empty_like(bt) for _ in range(nbuf)]
+    in_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    decoded = [torch.cuda.Event() for _ in range(nbuf)]
 
-    def e2e_step():
-        qd = q_h.to(device, non_blocking=True)
-        ld = lens_h.to(device, non_blocking=True)
-        bd = bt_h.to(device, non_blocking=True)
-        o, l = mla_decode(qd, kv, ld, bd, softmax_scale=SCALE, num_splits=splits, return_lse=True,
-                          kernel=args.kernel, plan=plan)
-        out_h.copy_(o, non_blocking=True)
-        lse_h.copy_(l, non_blocking=True)
+    def e2e_steps(n):
+        for i in range(n):
+            k = i % nbuf
+            with torch.cuda.stream(s_in):
+                if i >= nbuf:
+                    s_in.wait_event(decoded[k])  # the decode of step i - nbuf has read buffer set k
+                q_d[k].copy_(q_h, non_blocking=True)
+                lens_d[k].copy_(lens_h, non_blocking=True)
+                bt_d[k].copy_(bt_h, non_blocking=True)
+                in_ready[k].record(s_in)
+            stream.wait_event(in_ready[k])
+            flush.zero_()
+            o, l = mla_decode(q_d[k], kv, lens_d[k], bt_d[k], softmax_scale=SCALE, num_splits=splits,
+                              return_lse=True, kernel=args.kernel, plan=plan)
+            decoded[k].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(decoded[k])
+                out_h[k].copy_(o, non_blocking=True)
+                lse_h[k].copy_(l, non_blocking=True)
+            o.record_stream(s_out)
+            l.record_stream(s_out)
 
-    for _ in range(args.warmup):
-        e2e_step()
+    e2e_steps(args.warmup)
     torch.cuda.synchronize()
-    e_ms = []
-    for _ in range(args.steps):
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s_in)
+    e2e_steps(args.steps)
+    s_out.wait_stream(stream)
+    s_out.wait_stream(s_in)
+    b.record(s_out)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / args.steps
+    # one step at a time (no overlap between steps), for the latency of a single call
+    lat = []
+    for _ in range(min(args.steps, 10)):
         flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        e2e_step()
-        b.record(stream)
-        b.synchronize()
-        e_ms.append(a.elapsed_time(b))
-    e2e_ms = sum(e_ms) / len(e_ms)
-    te = torch.tensor([e2e_ms], device=device)
+        torch.cuda.synchronize()
+        a.record(s_in)
+        e2e_steps(1)
+        s_out.wait_stream(stream)
+        b.record(s_out)
+        torch.cuda.synchronize()
+        lat.append(a.elapsed_time(b))
+    te = torch.tensor([e2e_ms, sum(lat) / len(lat)], device=device)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
+    e2e_ms, e2e_lat_ms = float(te[0].item()), float(te[1].item())
 
     if world > 1:
         dist.barrier()
@@ -630,7 +742,10 @@ def main(argv=None):
         "cpu_baseline": cpu,
         "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "per step: q, seqlens, block_table host->device; out, lse device->host; cache resident"},
+                "latency_ms_one_step": e2e_lat_ms,
+                "note": "per step: q, seqlens, block_table host->device from pinned memory, L2 flush, mla_decode, "
+                        "out and lse device->host; cache resident; steps pipelined over an upload, a compute "
+                        "and a download stream (K steps from the first upload to the last download)"},
         "gpu_launches": gpu_launches,
         "clocks": clocks.summary(),
     }
