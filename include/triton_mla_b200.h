@@ -140,6 +140,19 @@ size_t tmla_units_workspace_bytes(int32_t num_slots, int32_t num_heads, int32_t 
 int tmla_decode_units(const TmlaDecodeParams* p, const int32_t* units, const int32_t* req_first,
                       int32_t num_units, int32_t num_slots, void* stream);
 
+/* Per-request split plan computed on the GPU, in `stream`, from the lengths in device memory
+   (no host sync; a plan kernel, tmla_decode_units and its merge can be captured in one CUDA
+   graph and replayed as the lengths change).  Writes `capacity` units (device int4
+   [capacity]) and req_first (device int32 [batch + 1]) in the layout of tmla_plan_units;
+   entries past the plan's own units are {-1, 0, 0, -1}, and their clusters exit at once.
+   The plan uses at most `slot_capacity` partial slots.  Pass num_units = capacity and
+   num_slots = slot_capacity to tmla_decode_units (workspace: tmla_units_workspace_bytes of
+   slot_capacity).  Requires batch <= capacity <= 65535.  The reference has no counterpart:
+   its num_splits=None reads max(cache_seqlens) on the host (kernel.py:264-266). */
+int tmla_plan_units_device(const int32_t* seqlens, int32_t batch, int32_t num_heads, int32_t num_sms,
+                           int32_t capacity, int32_t slot_capacity, int32_t* units, int32_t* req_first,
+                           void* stream);
+
 /* Stage 1 only: writes ws_o / ws_lse for every (request, head, split).
    Replaces the `_mla_decode_stage1` launch (kernel.py:276-302). */
 int tmla_decode_partial(const TmlaDecodeParams* p, void* stream);

@@ -202,3 +202,20 @@ def test_plan_units_edge_cases():
     lib = _lib.load()
     bad = np.zeros(4, dtype=np.int32)
     assert lib.tmla_plan_units(None, 2, 128, 148, 8, bad.ctypes.data, bad.ctypes.data) < 0
+
+
+def test_plan_units_device_rejects_bad_arguments():
+    """tmla_plan_units_device checks its arguments before it launches anything."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)  # never dereferenced: every call below is rejected first
+    bad = [
+        (p, 4, 128, 148, 3, 0, p, p),        # capacity below the batch (one unit per request at least)
+        (p, 4, 128, 148, 65536, 0, p, p),    # capacity above the grid limit
+        (p, 4, 128, 148, 8, -1, p, p),       # negative slot capacity
+        (p, 4, 0, 148, 8, 0, p, p),          # no heads
+        (p, 4, 128, 148, 8, 0, p, None),     # no req_first
+        (None, 4, 128, 148, 8, 0, p, p),     # no lengths
+        (p, -1, 128, 148, 8, 0, p, p),       # negative batch
+    ]
+    for args in bad:
+        assert lib.tmla_plan_units_device(*args, None) == _lib.ERR_INVALID_ARG, args

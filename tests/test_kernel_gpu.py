@@ -423,3 +423,124 @@ def test_split_plan_reused_across_lengths_and_in_a_graph(device):
         check(e_out, e_lse, ref_out, ref_lse, new)
         check(g_out, g_lse, ref_out, ref_lse, new)
     del graph
+
+
+# ----------------------------------------------------------------------------- device-side split plans
+# tmla_plan_units_device plans on the GPU from the lengths in device memory: a table of fixed
+# capacity (padding entries {-1, 0, 0, -1}), so planning and decode can be captured together.
+def _device_plan_host_view(plan):
+    units = plan.units.cpu().numpy()
+    first = plan.req_first.cpu().numpy()
+    real = units[units[:, 0] >= 0]
+    pad = units[units[:, 0] < 0]
+    return units, real, pad, first
+
+
+def _check_device_plan(lens, plan):
+    units, real, pad, first = _device_plan_host_view(plan)
+    lens = np.asarray(lens)
+    tiles = (np.maximum(lens, 0) + 63) // 64
+    assert len(real) + len(pad) == plan.num_units and len(real) >= len(lens)
+    assert np.all(units[len(real):, 0] < 0), "padding entries come after the plan's units"
+    assert np.all(pad == np.array([-1, 0, 0, -1]))
+    seen = {}
+    for b, s, ns, slot in real.tolist():
+        assert 0 <= b < len(lens) and 1 <= ns <= 64 and 0 <= s < ns and (b, s) not in seen
+        seen[(b, s)] = ns
+        assert slot == (-1 if ns == 1 else first[b] + s)
+    for b in range(len(lens)):
+        ns = seen[(b, 0)]
+        assert all(seen.get((b, s)) == ns for s in range(ns)), f"request {b} misses a split"
+        assert first[b + 1] - first[b] == (ns if ns > 1 else 0)
+    assert first[0] == 0 and first[-1] <= plan.num_slots
+    # longest first, up to the planner's bucket width (1/127 of the longest unit)
+    sizes = []
+    for b, s, ns, _ in real.tolist():
+        per = -(-int(tiles[b]) // ns)
+        sizes.append(max(0, min(int(tiles[b]), (s + 1) * per) - min(int(tiles[b]), s * per)))
+    slack = max(sizes) // 127 + 1 if sizes else 0
+    assert all(sizes[i] + slack >= sizes[i + 1] for i in range(len(sizes) - 1))
+    return real
+
+
+@pytest.mark.parametrize("lens", [
+    [4096] * 32,
+    [65536] * 4,
+    [60000] + [0] * 300 + [37] * 700,
+    [0, 0, 0],
+    [1],
+])
+def test_device_plan_is_a_valid_plan(device, lens):
+    from triton_mla import make_device_split_plan
+    from triton_mla.kernel import plan_units
+    plan = make_device_split_plan(torch.tensor(lens, dtype=torch.int32, device=device), 128)
+    real = _check_device_plan(lens, plan)
+    if len(set(lens)) == 1 and lens[0] >= 4096:
+        host, _ = plan_units(lens, 128)
+        assert set(real[:, 2].tolist()) == set(host[:, 2].tolist()), "uniform batches: the host planner's split"
+    if lens[0] == 60000:
+        assert real[real[:, 0] == 0][0, 2] > 1, "the long request is split"
+
+
+def test_device_plan_on_ragged_batches(device):
+    from triton_mla import make_device_split_plan
+    rng = np.random.default_rng(1)
+    g = torch.Generator().manual_seed(0)
+    batches = [torch.randint(1, 16385, (256,), generator=g).tolist()]
+    batches += [rng.integers(0, 20000, size=int(rng.integers(1, 400))).tolist() for _ in range(8)]
+    for lens in batches:
+        plan = make_device_split_plan(torch.tensor(lens, dtype=torch.int32, device=device), 128)
+        _check_device_plan(lens, plan)
+        small = make_device_split_plan(torch.tensor(lens, dtype=torch.int32, device=device), 128,
+                                       capacity=len(lens), slot_capacity=0)
+        real = _check_device_plan(lens, small)
+        assert set(real[:, 2].tolist()) == {1}, "no room for splits: one unit per request"
+
+
+@pytest.mark.parametrize("lens,num_heads", [
+    ([4096, 1000, 0, 65, 3000, 64, 1, 7777], 128),
+    ([65536, 100, 200, 0, 37], 128),
+    ([2048, 100, 5000, 1, 64, 9000], 200),
+])
+def test_device_plan_decode_matches_reference(device, lens, num_heads):
+    from triton_mla import make_device_split_plan
+    case = recipes.paged_case(lens, num_heads, 64, seed=23)
+    c = to_dev(case, device)
+    plan = make_device_split_plan(c["seqlens"], num_heads)
+    out, lse = mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          return_lse=True, plan=plan)
+    ref_out, ref_lse = oracle_of(case)
+    check(out, lse, ref_out, ref_lse, lens)
+    assert read_status(device) == 0
+
+
+def test_device_plan_and_decode_in_one_graph(device):
+    """The plan kernel, the split kernel and the merge captured together, replayed while the
+    lengths change (each replay re-plans from the lengths then in memory)."""
+    from triton_mla import make_device_split_plan
+    lens0 = [4096, 100, 0, 7000, 33, 20000]
+    case = recipes.paged_case(lens0, 128, 64, seed=31)
+    c = to_dev(case, device)
+    lens = c["seqlens"].clone()
+    plan = make_device_split_plan(lens, 128)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        plan.refresh(lens)
+        mla_decode(c["q"], c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True, plan=plan)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        plan.refresh(lens)
+        g_out, g_lse = mla_decode(c["q"], c["kv"], lens, c["block_table"], softmax_scale=c["scale"],
+                                  return_lse=True, plan=plan)
+    for new in (lens0, [20000, 1, 1, 1, 1, 1], [0, 0, 0, 0, 0, 64], [5000, 5000, 5000, 5000, 5000, 5000]):
+        lens.copy_(torch.tensor(new, dtype=torch.int32, device=device))
+        graph.replay()
+        torch.cuda.synchronize(device)
+        sub = dict(case, seqlens=torch.tensor(new, dtype=torch.int32))
+        ref_out, ref_lse = oracle_of(sub)
+        check(g_out, g_lse, ref_out, ref_lse, new)
+        _check_device_plan(new, plan)
+        assert read_status(device) == 0
+    del graph

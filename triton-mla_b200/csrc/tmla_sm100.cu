@@ -368,6 +368,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   int split = blockIdx.y, b = blockIdx.z, nsplit = p.num_splits, slot = -1;
   if (args.units) {
     const int4 un = __ldg(args.units + blockIdx.z);
+    // A padding entry of a fixed-capacity plan (tmla_plan_units_device): both CTAs of the
+    // cluster read the same entry and leave before touching any barrier or the peer.
+    if (un.x < 0) return;
     b = un.x, split = un.y, nsplit = un.z, slot = un.w;
   }
   // One split writes the final output (and natural-log LSE); several write fp32 partials.

@@ -6,7 +6,8 @@ Exports the same names as the reference package (src/triton_mla/__init__.py:1-14
 """
 
 from . import layer_ops, sharding
-from .kernel import SplitPlan, get_num_splits, make_split_plan, mla_decode, read_status, selected_kernel
+from .kernel import (SplitPlan, get_num_splits, make_device_split_plan, make_split_plan, mla_decode, read_status,
+                     selected_kernel)
 from .model import MLA, MLAConfig, MLADecodeGraph
 from .reference import mla_decode_ref, mla_decode_torch
 
@@ -18,6 +19,7 @@ __all__ = [
     "MLADecodeGraph",
     "SplitPlan",
     "get_num_splits",
+    "make_device_split_plan",
     "make_split_plan",
     "mla_decode",
     "mla_decode_ref",

@@ -58,6 +58,7 @@ EXPORTED = (
     "tmla_plan_units",
     "tmla_units_workspace_bytes",
     "tmla_decode_units",
+    "tmla_plan_units_device",
 )
 
 
@@ -221,6 +222,8 @@ def load() -> ctypes.CDLL:
     lib.tmla_units_workspace_bytes.restype = ctypes.c_size_t
     lib.tmla_decode_units.argtypes = [P, vp, vp, i32, i32, vp]
     lib.tmla_decode_units.restype = ctypes.c_int
+    lib.tmla_plan_units_device.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp, vp]
+    lib.tmla_plan_units_device.restype = ctypes.c_int
     for name, st in (("tmla_q_absorb_rope", TmlaQPrepParams), ("tmla_kv_norm_rope_append", TmlaKvAppendParams),
                      ("tmla_o_unabsorb", TmlaOUnabsorbParams)):
         fn = getattr(lib, name)

@@ -10,9 +10,10 @@ reference's ``triton_mla.mla_decode`` (src/triton_mla/kernel.py:204-323):
 * ``block_table is None`` selects the dense ``[B, S_max, D]`` layout (kernel.py:257-262);
 * ``num_splits=None`` costs one host sync to read the longest request
   (kernel.py:264-266); an explicit value keeps the call sync-free (CUDA-graph safe).
-  Inside CUDA-graph capture, where the reference's sync would fail, ``None`` sizes the
-  split count for the longest request the cache can hold (no sync): the kernels read
-  the actual lengths on the device, so the captured call stays valid when the lengths
+  Inside CUDA-graph capture, where the reference's sync would fail, ``None`` plans the
+  splits on the GPU from the lengths at replay time (tcgen05 kernel;
+  ``make_device_split_plan``), or sizes the split count for the longest request the cache
+  can hold (generic kernel).  Either way the captured call stays valid when the lengths
   change between replays;
 * returns ``out [B, H, head_dim_v]`` in ``q.dtype`` and, with ``return_lse``,
   the natural-log LSE ``[B, H]`` fp32; zero-length requests give 0 and -inf.
@@ -75,6 +76,11 @@ class SplitPlan:
     where the splits start: the kernels cut each request's tokens from its length on the
     device.  So a plan stays valid when the lengths change (a decode loop can plan once per
     batch composition) and a call with a plan needs no host sync (CUDA-graph safe).
+
+    A host plan (``make_split_plan``) holds exactly its units.  A device plan
+    (``make_device_split_plan``) holds a fixed number of entries (``num_units`` is its
+    capacity, padding entries do no work) and ``num_slots`` partial slots, and
+    ``refresh`` re-plans it on the GPU for new lengths.
     """
 
     def __init__(self, units, req_first, device):
@@ -83,7 +89,45 @@ class SplitPlan:
         self.num_slots = int(req_first[-1])
         self.units = torch.from_numpy(units).to(device)
         self.req_first = torch.from_numpy(req_first).to(device)
-        self.splits = units[:, 2].copy()  # per unit, on the host
+        self.num_heads = None
+
+    @classmethod
+    def empty(cls, batch: int, num_heads: int, capacity: int, slot_capacity: int, device) -> "SplitPlan":
+        plan = cls.__new__(cls)
+        plan.batch, plan.num_units, plan.num_slots, plan.num_heads = batch, capacity, slot_capacity, num_heads
+        plan.units = torch.empty(capacity, 4, dtype=torch.int32, device=device)
+        plan.req_first = torch.empty(batch + 1, dtype=torch.int32, device=device)
+        return plan
+
+    def refresh(self, cache_seqlens: torch.Tensor) -> "SplitPlan":
+        """Re-plan a device plan for the lengths now in ``cache_seqlens`` (int32, on the plan's
+        device), on the current stream: one small kernel, no host sync, capturable."""
+        if self.num_heads is None:
+            raise ValueError("refresh() re-plans a device plan (make_device_split_plan)")
+        assert cache_seqlens.shape == (self.batch,) and cache_seqlens.device == self.units.device
+        lens = cache_seqlens.to(torch.int32).contiguous()
+        dev = self.units.device
+        _lib.check(_lib.load().tmla_plan_units_device(
+            lens.data_ptr(), self.batch, self.num_heads, _num_sms(dev), self.num_units, self.num_slots,
+            self.units.data_ptr(), self.req_first.data_ptr(),
+            ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)), "tmla_plan_units_device")
+        return self
+
+
+def make_device_split_plan(cache_seqlens: torch.Tensor, num_heads: int, capacity: int | None = None,
+                           slot_capacity: int | None = None) -> SplitPlan:
+    """Plan per-request splits on the GPU from the lengths in device memory
+    (``tmla_plan_units_device``): no host sync, so the planning can sit in a CUDA graph with
+    the decode.  ``capacity`` work units (default: batch + 2 x the clusters that run at once)
+    and ``slot_capacity`` partial slots (default: 2 x those clusters) bound the plan and the
+    workspace; a plan that needs more falls back to fewer splits."""
+    dev = cache_seqlens.device
+    batch = int(cache_seqlens.shape[0])
+    machines = max(1, _num_sms(dev) // 2 // ((int(num_heads) + 127) // 128))
+    capacity = min(65535, batch + 2 * machines) if capacity is None else int(capacity)
+    slot_capacity = 2 * machines if slot_capacity is None else int(slot_capacity)
+    plan = SplitPlan.empty(batch, int(num_heads), capacity, slot_capacity, dev)
+    return plan.refresh(cache_seqlens)
 
 
 def make_split_plan(cache_seqlens, num_heads: int, device=None) -> SplitPlan:
@@ -244,9 +288,16 @@ def mla_decode(
         num_splits = 1
     elif num_splits is None:
         if batch > 0 and torch.cuda.is_current_stream_capturing():
-            # No host sync during capture: size the splits for the longest request the cache holds.
-            max_seqlen = bt_width * page_size if paged else kv_cache.shape[1]
-            num_splits = get_num_splits(batch, num_heads, max_seqlen, _num_sms(device))
+            # No host sync during capture.  The tcgen05 kernel follows a plan made on the GPU
+            # from the lengths at replay time; the generic kernel's split count is sized for
+            # the longest request the cache holds.
+            if kernel != "generic" and selected_kernel(q, kv_cache, block_table, head_dim_v, num_splits=1,
+                                                       kernel=kernel) == "sm100":
+                plan = make_device_split_plan(cache_seqlens, num_heads)
+                num_splits = 1
+            else:
+                max_seqlen = bt_width * page_size if paged else kv_cache.shape[1]
+                num_splits = get_num_splits(batch, num_heads, max_seqlen, _num_sms(device))
         elif batch > 0:
             # The one host sync (the reference reads max(cache_seqlens) here, kernel.py:264-266).
             lens_host = cache_seqlens.cpu()
