@@ -194,6 +194,12 @@ size_t tmla_params_bytes(void);
 /* q_out[b, h, :] = [ q_in[b, h, :d_nope] . W_UK[h]  |  rope(q_in[b, h, d_nope:], positions[b]) ]:
    the decode query from wq_b's output (model.py:111-113 with the q_pe RoPE of model.py:78).
    Needs rank even and w_kv_b 8-byte aligned (else TMLA_ERR_MISALIGNED); d_nope <= 512. */
+/* Layer-op flag: launch as a programmatic dependent of the preceding kernel in the stream
+   (its launch and the op's weight-tile loads overlap that kernel's end; every input other
+   than the weights is read only after that kernel has completed).  Do not set it when the
+   preceding kernel writes w_kv_b / norm_weight. */
+#define TMLA_LAYER_FLAG_PDL 1
+
 typedef struct TmlaQPrepParams {
   const void* q_in;                /* [batch, heads, d_nope + d_rope] */
   int64_t q_in_stride_b, q_in_stride_h;
@@ -204,6 +210,7 @@ typedef struct TmlaQPrepParams {
   int32_t batch, num_heads, d_nope, d_rope, d_v, rank;
   int32_t dtype;
   float rope_theta;
+  int32_t flags;                   /* TMLA_LAYER_FLAG_* */
 } TmlaQPrepParams;
 int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream);
 
@@ -228,6 +235,7 @@ typedef struct TmlaKvAppendParams {
   int32_t batch, rank, d_rope;
   int32_t dtype;
   float eps, rope_theta;
+  int32_t flags;                   /* TMLA_LAYER_FLAG_* */
 } TmlaKvAppendParams;
 int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream);
 
@@ -242,6 +250,7 @@ typedef struct TmlaOUnabsorbParams {
   int64_t out_stride_b;
   int32_t batch, num_heads, d_nope, d_v, rank;
   int32_t dtype;
+  int32_t flags;                   /* TMLA_LAYER_FLAG_* */
 } TmlaOUnabsorbParams;
 int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream);
 

@@ -24,13 +24,14 @@ def _close(got, ref, dtype):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("batch,heads", [(1, 16), (16, 128), (37, 20)])
-def test_q_absorb_rope_matches_torch(device, dtype, batch, heads):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_q_absorb_rope_matches_torch(device, dtype, batch, heads, overlap):
     g = torch.Generator(device=device).manual_seed(batch * 131 + heads)
     dn, dr, dv, r = 128, 64, 128, 512
     q = torch.randn(batch, heads, dn + dr, generator=g, device=device).to(dtype)
     w = (torch.randn(heads * (dn + dv), r, generator=g, device=device) * 0.05).to(dtype)
     pos = torch.randint(0, 20000, (batch,), generator=g, device=device, dtype=torch.int32)
-    got = layer_ops.q_absorb_rope(q, w, pos, dn, dv, 10000.0)
+    got = layer_ops.q_absorb_rope(q, w, pos, dn, dv, 10000.0, overlap=overlap)
     w_uk = w.view(heads, dn + dv, r)[:, :dn]
     ref_abs = torch.einsum("bhd,hdc->bhc", q[..., :dn].float(), w_uk.float())
     ref_pe = apply_rope(q[..., dn:].float(), pos[:, None], 10000.0)
@@ -40,7 +41,8 @@ def test_q_absorb_rope_matches_torch(device, dtype, batch, heads):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("paged", [True, False])
-def test_kv_norm_rope_append_matches_torch(device, dtype, paged):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_kv_norm_rope_append_matches_torch(device, dtype, paged, overlap):
     g = torch.Generator(device=device).manual_seed(5)
     batch, r, dr, page = 9, 512, 64, 16
     kva = torch.randn(batch, r + dr, generator=g, device=device).to(dtype)
@@ -55,7 +57,7 @@ def test_kv_norm_rope_append_matches_torch(device, dtype, paged):
         cache = torch.randn(batch, 256, r + dr, generator=g, device=device).to(dtype)
     before = cache.clone()
     seq = torch.empty_like(pos)
-    layer_ops.kv_norm_rope_append(kva, wn, pos, cache, bt, 1e-6, 10000.0, seqlens_out=seq)
+    layer_ops.kv_norm_rope_append(kva, wn, pos, cache, bt, 1e-6, 10000.0, seqlens_out=seq, overlap=overlap)
     torch.cuda.synchronize()
     assert torch.equal(seq, pos + 1)
     rows = torch.arange(batch, device=device)
@@ -87,12 +89,13 @@ def test_kv_append_past_the_cache_is_flagged_and_dropped(device):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("batch", [1, 16, 33])
-def test_o_unabsorb_matches_torch(device, dtype, batch):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_o_unabsorb_matches_torch(device, dtype, batch, overlap):
     g = torch.Generator(device=device).manual_seed(batch)
     heads, dn, dv, r = 128, 128, 128, 512
     o = torch.randn(batch, heads, r, generator=g, device=device).to(dtype)
     w = (torch.randn(heads * (dn + dv), r, generator=g, device=device) * 0.05).to(dtype)
-    got = layer_ops.o_unabsorb(o, w, dn, dv)
+    got = layer_ops.o_unabsorb(o, w, dn, dv, overlap=overlap)
     w_uv = w.view(heads, dn + dv, r)[:, dn:]
     ref = torch.einsum("bhc,hdc->bhd", o.float(), w_uv.float()).reshape(batch, heads * dv)
     _close(got, ref, dtype)

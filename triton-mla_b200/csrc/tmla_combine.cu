@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
                            int DV) {
   // Launched as a programmatic dependent of the split kernel: wait for its partials.
   ptx::griddep_wait();
+  ptx::griddep_launch_dependents();  // a programmatic successor may be scheduled now
   const int lane = threadIdx.x & 31;
   const int groups = DV / 128;
   const int64_t wid = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
@@ -116,6 +117,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
                              const int32_t* __restrict__ req_first, T* __restrict__ out, int64_t osb, int64_t osh,
                              float* __restrict__ lse, int64_t lsb, int B, int H, int DV) {
   ptx::griddep_wait();
+  ptx::griddep_launch_dependents();  // a programmatic successor may be scheduled now
   const int lane = threadIdx.x & 31;
   const int groups = DV / 128;
   const int64_t wid = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
@@ -170,6 +172,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     mla_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
                        int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S, int DV) {
   ptx::griddep_wait();
+  ptx::griddep_launch_dependents();  // a programmatic successor may be scheduled now
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
   if (row >= (int64_t)B * H) return;

@@ -14,9 +14,18 @@
 // angle = pos * theta^(-2i / d_rope), out[i] = a cos - b sin, out[i + d_rope/2] =
 // b cos + a sin with a = x[i], b = x[i + d_rope / 2].
 #include "tmla_common.cuh"
+#include "tmla_ptx.cuh"
 
 namespace tmla {
 namespace layer {
+
+// Launched with TMLA_LAYER_FLAG_PDL, a kernel may start while the preceding kernel in the
+// stream is finishing: it loads only weights before this point, then waits for that kernel
+// (a no-op in an ordinary launch) and lets the next programmatic launch be scheduled.
+__device__ __forceinline__ void after_predecessor() {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+}
 
 template <typename T>
 __device__ __forceinline__ float ld(const T* p) {
@@ -145,6 +154,7 @@ __global__ void __launch_bounds__(128) q_absorb_rope_kernel(TmlaQPrepParams p) {
   constexpr int kEpv = 16 / (int)sizeof(T);  // elements per 16-byte vector
   const bool q_vec = dn % kEpv == 0 && (p.q_in_stride_b * (int)sizeof(T)) % 16 == 0 &&
                      (p.q_in_stride_h * (int)sizeof(T)) % 16 == 0 && (uintptr_t)q_in % 16 == 0;
+  after_predecessor();
   for (int b0 = 0; b0 < p.batch; b0 += kBChunk) {
     __syncthreads();
     if (q_vec) {
@@ -223,6 +233,7 @@ __global__ void __launch_bounds__(128) q_absorb_rope_kernel(TmlaQPrepParams p) {
 // One warp per request.
 template <typename T>
 __global__ void __launch_bounds__(128) kv_append_kernel(TmlaKvAppendParams p) {
+  after_predecessor();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x * 4 + warp;
   if (b >= p.batch) return;
@@ -245,16 +256,72 @@ __global__ void __launch_bounds__(128) kv_append_kernel(TmlaKvAppendParams p) {
     return;
   }
   T* dst = static_cast<T*>(p.kv_cache) + page * p.kv_stride_page + slot * p.kv_stride_tok;
-  float ss = 0.f;
-  for (int e = lane; e < R; e += 32) {
-    const float x = ld(src + e);
-    ss = fmaf(x, x, ss);
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rstd = rsqrtf(ss / (float)R + p.eps);
   const T* wn = static_cast<const T*>(p.norm_weight);
-  for (int e = lane; e < R; e += 32) dst[e] = cvt<T>(ld(src + e) * rstd * ld(wn + e));
+  // 16-bit rows with 16-byte alignment: every lane issues its 16-byte loads of the latent
+  // row and of the norm weight at once (at most 8 each, rank <= 2048), then normalises.
+  constexpr int kMaxVec = 8;
+  bool done = false;
+  if constexpr (sizeof(T) == 2) {
+    if (R % 8 == 0 && R <= 8 * 32 * kMaxVec && ((uintptr_t)src % 16) == 0 && ((uintptr_t)wn % 16) == 0 &&
+        ((uintptr_t)dst % 16) == 0) {
+      done = true;
+      const int nvec = R / 8;
+      uint4 xv[kMaxVec], wv[kMaxVec];
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) {
+          xv[i] = reinterpret_cast<const uint4*>(src)[c];
+          wv[i] = reinterpret_cast<const uint4*>(wn)[c];
+        }
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        if (lane + 32 * i < nvec) {
+          const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float a, b;
+            unpack2(xw[j], src, a, b);
+            ss = fmaf(a, a, fmaf(b, b, ss));
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss / (float)R + p.eps);
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) {
+          const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+          const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float xa, xb, wa, wb;
+            unpack2(xw[j], src, xa, xb);
+            unpack2(ww[j], src, wa, wb);
+            const T pr[2] = {cvt<T>(xa * rstd * wa), cvt<T>(xb * rstd * wb)};
+            ow[j] = *reinterpret_cast<const uint32_t*>(pr);
+          }
+          reinterpret_cast<uint4*>(dst)[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+    }
+  }
+  if (!done) {
+    float ss = 0.f;
+    for (int e = lane; e < R; e += 32) {
+      const float x = ld(src + e);
+      ss = fmaf(x, x, ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rstd = rsqrtf(ss / (float)R + p.eps);
+    for (int e = lane; e < R; e += 32) dst[e] = cvt<T>(ld(src + e) * rstd * ld(wn + e));
+  }
   for (int k = lane; k < half; k += 32) {
     float oa, ob;
     rope_pair(ld(src + R + k), ld(src + R + k + half), pos, k, dr, p.rope_theta, oa, ob);
@@ -280,6 +347,7 @@ __global__ void __launch_bounds__(128) o_unabsorb_kernel(TmlaOUnabsorbParams p) 
   const T* w = static_cast<const T*>(p.w_kv_b) + ((int64_t)h * (dn + dv) + dn + d0) * R;  // W_UV[h][d0:]
   const int vpr = R * (int)sizeof(T) / 16;
   stage_rows16(ws, stride, w, R, nd, vpr);
+  after_predecessor();
   const bool o_vec = (p.o_stride_b * (int)sizeof(T)) % 16 == 0 && (p.o_stride_h * (int)sizeof(T)) % 16 == 0 &&
                      ((uintptr_t)o % 16) == 0;
   const int dd = tid & 15, bh = tid >> 4;  // v row d0 + dd; requests bh and bh + 8 of the chunk
@@ -398,6 +466,7 @@ __global__ void __launch_bounds__(128) q_absorb_rope_mma_kernel(TmlaQPrepParams 
   T* q_out = static_cast<T*>(p.q_out);
   stage_rows16(ws, kWs, static_cast<const T*>(p.w_kv_b) + (int64_t)h * (dn + p.d_v) * R + c0, R, dn,
                kCols * (int)sizeof(T) / 16);
+  after_predecessor();
   for (int b0 = 0; b0 < p.batch; b0 += kBChunk) {
     __syncthreads();
     stage_batch_rows(qs, qstride, q_in, p.q_in_stride_b, p.q_in_stride_h, h, b0, p.batch, dn);
@@ -442,54 +511,50 @@ __global__ void __launch_bounds__(128) q_absorb_rope_mma_kernel(TmlaQPrepParams 
   }
 }
 
-// o: grid (heads, d_v / 16), 128 threads.  M = 16 rows of W_UV, N = 16 requests, K = rank
-// split over the 4 warps (partial sums added through shared memory).  A = W_UV rows
-// (row-major), B = o rows (c contiguous, i.e. col-major).
+// o: grid (heads, d_v / 32), 128 threads.  The CTA computes 32 rows of W_UV[h] (d) x 16
+// requests; warp w owns the 16 x 8 tile (d rows 16 (w & 1) .., requests 8 (w >> 1) ..) over
+// the whole K = rank, so no partial sums cross warps.  A = W_UV rows (row-major), B = o rows
+// (c contiguous, i.e. col-major).  Shared memory (32 + 16 rows of rank + 8 elements, 50 KB
+// at rank 512) lets 4 CTAs share an SM, so DeepSeek's 128 x 4 CTAs run in one wave.
 template <typename T>
 __global__ void __launch_bounds__(128) o_unabsorb_mma_kernel(TmlaOUnabsorbParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int R = p.rank, stride = R + 8, dn = p.d_nope, dv = p.d_v, d0 = blockIdx.y * 16;
-  T* ws = reinterpret_cast<T*>(smem);  // [16][stride]
-  T* os = ws + 16 * stride;            // [16][stride]
-  float* red = reinterpret_cast<float*>(os + 16 * stride);  // [4 warps][16 d][16 b]
+  const int R = p.rank, stride = R + 8, dn = p.d_nope, dv = p.d_v, d0 = blockIdx.y * 32;
+  T* ws = reinterpret_cast<T*>(smem);  // [32][stride]
+  T* os = ws + 32 * stride;            // [16][stride]
   const T* o = static_cast<const T*>(p.o);
   T* out = static_cast<T*>(p.out);
-  stage_rows16(ws, stride, static_cast<const T*>(p.w_kv_b) + ((int64_t)h * (dn + dv) + dn + d0) * R, R, 16,
+  stage_rows16(ws, stride, static_cast<const T*>(p.w_kv_b) + ((int64_t)h * (dn + dv) + dn + d0) * R, R, 32,
                R * (int)sizeof(T) / 16);
-  const int kq = R / 4;
+  after_predecessor();
+  const int mt = warp & 1, nt = warp >> 1;
+  const T* wrow = ws + (16 * mt) * stride;
   for (int b0 = 0; b0 < p.batch; b0 += kBChunk) {
     __syncthreads();
     stage_batch_rows(os, stride, o, p.o_stride_b, p.o_stride_h, h, b0, p.batch, R);
     __syncthreads();
-    float acc[2][4] = {};
-    for (int k0 = warp * kq; k0 < (warp + 1) * kq; k0 += 16) {
+    float acc[4] = {};
+    const T* orow = os + (nt * 8 + g) * stride;
+    for (int k0 = 0; k0 < R; k0 += 16) {
       uint32_t a[4];
-      a[0] = lds32(ws + g * stride + k0 + 2 * t);
-      a[1] = lds32(ws + (g + 8) * stride + k0 + 2 * t);
-      a[2] = lds32(ws + g * stride + k0 + 2 * t + 8);
-      a[3] = lds32(ws + (g + 8) * stride + k0 + 2 * t + 8);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const T* orow = os + (nt * 8 + g) * stride + k0 + 2 * t;
-        const uint32_t bf[2] = {lds32(orow), lds32(orow + 8)};
-        mma16816<T>(acc[nt], a, bf);
-      }
+      a[0] = lds32(wrow + g * stride + k0 + 2 * t);
+      a[1] = lds32(wrow + (g + 8) * stride + k0 + 2 * t);
+      a[2] = lds32(wrow + g * stride + k0 + 2 * t + 8);
+      a[3] = lds32(wrow + (g + 8) * stride + k0 + 2 * t + 8);
+      const uint32_t bf[2] = {lds32(orow + k0 + 2 * t), lds32(orow + k0 + 2 * t + 8)};
+      mma16816<T>(acc, a, bf);
     }
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      float* r = red + warp * 256;
-      r[g * 16 + nt * 8 + 2 * t] = acc[nt][0];
-      r[g * 16 + nt * 8 + 2 * t + 1] = acc[nt][1];
-      r[(g + 8) * 16 + nt * 8 + 2 * t] = acc[nt][2];
-      r[(g + 8) * 16 + nt * 8 + 2 * t + 1] = acc[nt][3];
+    // acc: D[d = g][b = 2t, 2t + 1], D[g + 8][2t, 2t + 1] of the warp's tile.
+    const int d = d0 + 16 * mt + g, b = b0 + 8 * nt + 2 * t;
+    T* col = out + (int64_t)h * dv;
+    if (b < p.batch) {
+      col[(int64_t)b * p.out_stride_b + d] = cvt<T>(acc[0]);
+      col[(int64_t)b * p.out_stride_b + d + 8] = cvt<T>(acc[2]);
     }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = threadIdx.x * 2 + k, d = i / 16, bb = i % 16, b = b0 + bb;
-      const float v = red[i] + red[256 + i] + red[512 + i] + red[768 + i];
-      if (b < p.batch) out[(int64_t)b * p.out_stride_b + (int64_t)h * dv + d0 + d] = cvt<T>(v);
+    if (b + 1 < p.batch) {
+      col[(int64_t)(b + 1) * p.out_stride_b + d] = cvt<T>(acc[1]);
+      col[(int64_t)(b + 1) * p.out_stride_b + d + 8] = cvt<T>(acc[3]);
     }
   }
 }
@@ -500,6 +565,23 @@ __global__ void __launch_bounds__(128) o_unabsorb_mma_kernel(TmlaOUnabsorbParams
 namespace {
 
 using namespace tmla::layer;
+
+// An ordinary launch, or a programmatic dependent of the preceding kernel in the stream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 int finish_launch() {
   const cudaError_t e = cudaGetLastError();
@@ -522,6 +604,7 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream) {
   const dim3 grid(p->num_heads, (p->rank + kCols - 1) / kCols), block(128);
   const size_t esz = p->dtype == TMLA_DTYPE_FP32 ? 4 : 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
   cudaError_t e = cudaSuccess;
   if (p->dtype != TMLA_DTYPE_FP32 && p->d_nope % 16 == 0 && p->rank % kCols == 0) {
     // 16-bit types: the contraction on tensor cores (mma.sync m16n8k16, fp32 accumulation).
@@ -529,11 +612,11 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream) {
     if (p->dtype == TMLA_DTYPE_BF16) {
       e = cudaFuncSetAttribute(q_absorb_rope_mma_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
-      if (e == cudaSuccess) q_absorb_rope_mma_kernel<__nv_bfloat16><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_mma_kernel<__nv_bfloat16>, grid, block, smem, s, *p);
     } else {
       e = cudaFuncSetAttribute(q_absorb_rope_mma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
-      if (e == cudaSuccess) q_absorb_rope_mma_kernel<__half><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_mma_kernel<__half>, grid, block, smem, s, *p);
     }
     if (e != cudaSuccess) return -(int)e;
     return finish_launch();
@@ -543,15 +626,15 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream) {
     case TMLA_DTYPE_BF16:
       e = cudaFuncSetAttribute(q_absorb_rope_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
-      if (e == cudaSuccess) q_absorb_rope_kernel<__nv_bfloat16><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_kernel<__nv_bfloat16>, grid, block, smem, s, *p);
       break;
     case TMLA_DTYPE_FP16:
       e = cudaFuncSetAttribute(q_absorb_rope_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) q_absorb_rope_kernel<__half><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_kernel<__half>, grid, block, smem, s, *p);
       break;
     default:
       e = cudaFuncSetAttribute(q_absorb_rope_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) q_absorb_rope_kernel<float><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_kernel<float>, grid, block, smem, s, *p);
   }
   if (e != cudaSuccess) return -(int)e;
   return finish_launch();
@@ -566,16 +649,19 @@ int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream) {
   if (p->block_table && p->bt_width <= 0) return TMLA_ERR_INVALID_ARG;
   const dim3 grid((p->batch + 3) / 4), block(128);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
+  cudaError_t e;
   switch (p->dtype) {
     case TMLA_DTYPE_BF16:
-      kv_append_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(*p);
+      e = launch(pdl, kv_append_kernel<__nv_bfloat16>, grid, block, 0, s, *p);
       break;
     case TMLA_DTYPE_FP16:
-      kv_append_kernel<__half><<<grid, block, 0, s>>>(*p);
+      e = launch(pdl, kv_append_kernel<__half>, grid, block, 0, s, *p);
       break;
     default:
-      kv_append_kernel<float><<<grid, block, 0, s>>>(*p);
+      e = launch(pdl, kv_append_kernel<float>, grid, block, 0, s, *p);
   }
+  if (e != cudaSuccess) return -(int)e;
   return finish_launch();
 }
 
@@ -590,17 +676,19 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream) {
   const dim3 grid(p->num_heads, (p->d_v + 15) / 16), block(128);
   const size_t esz = p->dtype == TMLA_DTYPE_FP32 ? 4 : 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
   cudaError_t e = cudaSuccess;
-  if (p->dtype != TMLA_DTYPE_FP32 && p->rank % 64 == 0 && p->d_v % 16 == 0) {
+  if (p->dtype != TMLA_DTYPE_FP32 && p->rank % 64 == 0 && p->d_v % 32 == 0) {
     // 16-bit types: the contraction on tensor cores (mma.sync m16n8k16, fp32 accumulation).
-    const size_t smem = (size_t)(16 + kBChunk) * (p->rank + 8) * esz + 4 * 256 * sizeof(float);
+    const dim3 grid_mma(p->num_heads, p->d_v / 32);
+    const size_t smem = (size_t)(32 + kBChunk) * (p->rank + 8) * esz;
     if (p->dtype == TMLA_DTYPE_BF16) {
       e = cudaFuncSetAttribute(o_unabsorb_mma_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem);
-      if (e == cudaSuccess) o_unabsorb_mma_kernel<__nv_bfloat16><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, o_unabsorb_mma_kernel<__nv_bfloat16>, grid_mma, block, smem, s, *p);
     } else {
       e = cudaFuncSetAttribute(o_unabsorb_mma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) o_unabsorb_mma_kernel<__half><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, o_unabsorb_mma_kernel<__half>, grid_mma, block, smem, s, *p);
     }
     if (e != cudaSuccess) return -(int)e;
     return finish_launch();
@@ -609,15 +697,15 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream) {
   switch (p->dtype) {
     case TMLA_DTYPE_BF16:
       e = cudaFuncSetAttribute(o_unabsorb_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) o_unabsorb_kernel<__nv_bfloat16><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, o_unabsorb_kernel<__nv_bfloat16>, grid, block, smem, s, *p);
       break;
     case TMLA_DTYPE_FP16:
       e = cudaFuncSetAttribute(o_unabsorb_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) o_unabsorb_kernel<__half><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, o_unabsorb_kernel<__half>, grid, block, smem, s, *p);
       break;
     default:
       e = cudaFuncSetAttribute(o_unabsorb_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess) o_unabsorb_kernel<float><<<grid, block, smem, s>>>(*p);
+      if (e == cudaSuccess) e = launch(pdl, o_unabsorb_kernel<float>, grid, block, smem, s, *p);
   }
   if (e != cudaSuccess) return -(int)e;
   return finish_launch();

@@ -23,6 +23,7 @@ ERR_UNSUPPORTED = 2
 ERR_MISALIGNED = 3
 ERR_CUDA = 4
 ERR_WORKSPACE = 5
+LAYER_FLAG_PDL = 1
 
 STATUS_BAD_PAGE = 0x1
 STATUS_TIMEOUT = 0x2
@@ -118,6 +119,7 @@ class TmlaQPrepParams(ctypes.Structure):
         ("rank", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("rope_theta", ctypes.c_float),
+        ("flags", ctypes.c_int32),
     ]
 
 
@@ -145,6 +147,7 @@ class TmlaKvAppendParams(ctypes.Structure):
         ("dtype", ctypes.c_int32),
         ("eps", ctypes.c_float),
         ("rope_theta", ctypes.c_float),
+        ("flags", ctypes.c_int32),
     ]
 
 
@@ -164,6 +167,7 @@ class TmlaOUnabsorbParams(ctypes.Structure):
         ("d_v", ctypes.c_int32),
         ("rank", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
     ]
 
 

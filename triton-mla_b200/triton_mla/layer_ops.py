@@ -37,23 +37,28 @@ def fusable(x: torch.Tensor, kv_cache: torch.Tensor, weights, rank: int, d_nope:
 
 
 def q_absorb_rope(q_in: torch.Tensor, w_kv_b: torch.Tensor, positions: torch.Tensor, d_nope: int, d_v: int,
-                  rope_theta: float) -> torch.Tensor:
-    """``[q_in[..., :d_nope] . W_UK | rope(q_in[..., d_nope:])]`` for q_in [batch, heads, d_nope + d_rope]."""
+                  rope_theta: float, overlap: bool = False) -> torch.Tensor:
+    """``[q_in[..., :d_nope] . W_UK | rope(q_in[..., d_nope:])]`` for q_in [batch, heads, d_nope + d_rope].
+
+    ``overlap``: launch as a programmatic dependent of the preceding kernel in the stream
+    (``TMLA_LAYER_FLAG_PDL``); that kernel must not write ``w_kv_b``."""
     batch, heads, d = q_in.shape
     rank = w_kv_b.shape[1]
     assert q_in.stride(-1) == 1 and positions.dtype == torch.int32 and positions.is_contiguous()
     q_out = torch.empty(batch, heads, rank + d - d_nope, dtype=q_in.dtype, device=q_in.device)
     p = _lib.TmlaQPrepParams(q_in.data_ptr(), q_in.stride(0), q_in.stride(1), w_kv_b.data_ptr(), positions.data_ptr(),
                              q_out.data_ptr(), q_out.stride(0), q_out.stride(1), batch, heads, d_nope, d - d_nope,
-                             d_v, rank, _DTYPE_CODES[q_in.dtype], float(rope_theta))
+                             d_v, rank, _DTYPE_CODES[q_in.dtype], float(rope_theta),
+                             _lib.LAYER_FLAG_PDL if overlap else 0)
     _lib.check(_lib.load().tmla_q_absorb_rope(ctypes.byref(p), _stream(q_in)), "tmla_q_absorb_rope")
     return q_out
 
 
 def kv_norm_rope_append(kv_in: torch.Tensor, norm_weight: torch.Tensor, positions: torch.Tensor,
                         kv_cache: torch.Tensor, block_table, eps: float, rope_theta: float,
-                        seqlens_out: torch.Tensor | None = None) -> None:
-    """Write ``[rmsnorm(kv_in[:, :rank]) | rope(kv_in[:, rank:])]`` at each request's position."""
+                        seqlens_out: torch.Tensor | None = None, overlap: bool = False) -> None:
+    """Write ``[rmsnorm(kv_in[:, :rank]) | rope(kv_in[:, rank:])]`` at each request's position.
+    ``overlap`` as in ``q_absorb_rope`` (the preceding kernel must not write ``norm_weight``)."""
     if kv_cache.dim() == 4:
         kv_cache = kv_cache.squeeze(2)
     batch, width = kv_in.shape
@@ -67,16 +72,19 @@ def kv_norm_rope_append(kv_in: torch.Tensor, norm_weight: torch.Tensor, position
         kv_cache.data_ptr(), kv_cache.stride(0), kv_cache.stride(1), kv_cache.shape[0], kv_cache.shape[1],
         _ptr(block_table), 0 if block_table is None else block_table.stride(0),
         0 if block_table is None else block_table.shape[1], _status_word(kv_in.device).data_ptr(),
-        batch, rank, width - rank, _DTYPE_CODES[kv_in.dtype], float(eps), float(rope_theta))
+        batch, rank, width - rank, _DTYPE_CODES[kv_in.dtype], float(eps), float(rope_theta),
+        _lib.LAYER_FLAG_PDL if overlap else 0)
     _lib.check(_lib.load().tmla_kv_norm_rope_append(ctypes.byref(p), _stream(kv_in)), "tmla_kv_norm_rope_append")
 
 
-def o_unabsorb(o: torch.Tensor, w_kv_b: torch.Tensor, d_nope: int, d_v: int) -> torch.Tensor:
-    """``o . W_UV`` per head for o [batch, heads, rank]; returns [batch, heads * d_v]."""
+def o_unabsorb(o: torch.Tensor, w_kv_b: torch.Tensor, d_nope: int, d_v: int, overlap: bool = False) -> torch.Tensor:
+    """``o . W_UV`` per head for o [batch, heads, rank]; returns [batch, heads * d_v].
+    ``overlap`` as in ``q_absorb_rope``."""
     batch, heads, rank = o.shape
     assert o.stride(-1) == 1
     out = torch.empty(batch, heads * d_v, dtype=o.dtype, device=o.device)
     p = _lib.TmlaOUnabsorbParams(o.data_ptr(), o.stride(0), o.stride(1), w_kv_b.data_ptr(), out.data_ptr(),
-                                 out.stride(0), batch, heads, d_nope, d_v, rank, _DTYPE_CODES[o.dtype])
+                                 out.stride(0), batch, heads, d_nope, d_v, rank, _DTYPE_CODES[o.dtype],
+                                 _lib.LAYER_FLAG_PDL if overlap else 0)
     _lib.check(_lib.load().tmla_o_unabsorb(ctypes.byref(p), _stream(o)), "tmla_o_unabsorb")
     return out

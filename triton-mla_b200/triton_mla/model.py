@@ -122,21 +122,34 @@ class MLA(nn.Module):
             return self._forward_fused(x, kv_cache, cache_seqlens, block_table, num_splits)
         return self._forward_ops(x, kv_cache, cache_seqlens, block_table, num_splits)
 
+    def _w_a(self):
+        """``[wq_a.weight; wkv_a.weight]``: both down-projections of x as one GEMM.  The copy
+        is cached and remade when either weight changes (storage or in-place version); a
+        captured CUDA graph keeps the copy it was captured with."""
+        wq, wkv = self.wq_a.weight, self.wkv_a.weight
+        key = (wq.data_ptr(), wq._version, wkv.data_ptr(), wkv._version, wq.dtype, wq.device)
+        if getattr(self, "_w_a_key", None) != key:
+            self._w_a_cat = torch.cat([wq.detach(), wkv.detach()], dim=0)
+            self._w_a_key = key
+        return self._w_a_cat
+
     def _forward_fused(self, x, kv_cache, cache_seqlens, block_table, num_splits):
         cfg = self.cfg
         batch = x.shape[0]
-        q = self.wq_b(self.q_norm(self.wq_a(x))).view(batch, cfg.num_heads, cfg.qk_head_dim)
-        kva = self.wkv_a(x)
+        qa, kva = F.linear(x, self._w_a()).split([cfg.q_lora_rank, cfg.kv_cache_dim], dim=-1)
+        q = self.wq_b(self.q_norm(qa)).view(batch, cfg.num_heads, cfg.qk_head_dim)
         positions = cache_seqlens.to(torch.int32).contiguous()
         bt = None if block_table is None else block_table.to(torch.int32).contiguous()
         seqlens = torch.empty_like(positions)
+        # The layer ops launch as programmatic dependents of the kernel before them (their
+        # weight loads and launch overlap its end): none of those kernels writes a weight.
         layer_ops.kv_norm_rope_append(kva, self.kv_norm.weight, positions, kv_cache, bt, self.kv_norm.eps,
-                                      cfg.rope_theta, seqlens_out=seqlens)
+                                      cfg.rope_theta, seqlens_out=seqlens, overlap=True)
         q_full = layer_ops.q_absorb_rope(q, self.wkv_b.weight, positions, cfg.qk_nope_head_dim, cfg.v_head_dim,
-                                         cfg.rope_theta)
+                                         cfg.rope_theta, overlap=True)
         o = mla_decode(q_full, kv_cache, seqlens, bt, head_dim_v=cfg.kv_lora_rank, softmax_scale=self.softmax_scale,
                        num_splits=num_splits)
-        o = layer_ops.o_unabsorb(o, self.wkv_b.weight, cfg.qk_nope_head_dim, cfg.v_head_dim)
+        o = layer_ops.o_unabsorb(o, self.wkv_b.weight, cfg.qk_nope_head_dim, cfg.v_head_dim, overlap=True)
         return self.wo(o), seqlens.to(cache_seqlens.dtype)
 
     def _forward_ops(self, x, kv_cache, cache_seqlens, block_table, num_splits):
