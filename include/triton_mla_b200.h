@@ -218,7 +218,10 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream);
    written at position positions[b] of request b (paged through block_table, or dense
    [batch, page_size, rank + d_rope] when block_table is NULL), and seqlens_out[b] =
    positions[b] + 1 when seqlens_out is not NULL (model.py:74-94, 116-117).  A position
-   past the cache or a page id outside the pool sets TMLA_STATUS_BAD_PAGE and drops the row. */
+   past the cache or a page id outside the pool sets TMLA_STATUS_BAD_PAGE and drops the row.
+   With q_in set, the same launch also writes q_out[b, :q_rank] = rmsnorm(q_in[b, :q_rank]) *
+   q_norm_weight (q_norm of the query path, model.py:75): both down-projections of x come out
+   of one GEMM, and its two halves are normalised here. */
 typedef struct TmlaKvAppendParams {
   const void* kv_in;               /* [batch, rank + d_rope]: wkv_a's output */
   int64_t kv_in_stride_b;
@@ -236,6 +239,13 @@ typedef struct TmlaKvAppendParams {
   int32_t dtype;
   float eps, rope_theta;
   int32_t flags;                   /* TMLA_LAYER_FLAG_* */
+  const void* q_in;                /* [batch, q_rank] (row stride q_in_stride_b) or NULL */
+  int64_t q_in_stride_b;
+  const void* q_norm_weight;       /* [q_rank] */
+  void* q_out;                     /* [batch, q_rank] (row stride q_out_stride_b) */
+  int64_t q_out_stride_b;
+  int32_t q_rank;
+  float q_eps;
 } TmlaKvAppendParams;
 int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream);
 

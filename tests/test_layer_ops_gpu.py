@@ -119,3 +119,25 @@ def test_fused_layer_step_equals_the_op_form(device, dtype, tol):
     assert torch.equal(seq_f, seq_o)
     torch.testing.assert_close(out_f.float(), out_o.float(), atol=tol, rtol=tol)
     torch.testing.assert_close(kv_a.float(), kv_b.float(), atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_kv_append_with_q_norm_matches_torch(device, dtype):
+    """The cache append and the query path's q_norm in one launch, from the two halves of one
+    GEMM output (strided rows)."""
+    g = torch.Generator(device=device).manual_seed(12)
+    batch, r, dr, qr, page = 7, 512, 64, 1536, 16
+    both = torch.randn(batch, qr + r + dr, generator=g, device=device).to(dtype)
+    qa, kva = both.split([qr, r + dr], dim=-1)
+    wn = (1 + 0.1 * torch.randn(r, generator=g, device=device)).to(dtype)
+    wq = (1 + 0.1 * torch.randn(qr, generator=g, device=device)).to(dtype)
+    pos = torch.randint(0, 100, (batch,), generator=g, device=device, dtype=torch.int32)
+    bt = torch.randperm(batch * 8, device=device).view(batch, 8).int()
+    cache = torch.zeros(batch * 8, page, r + dr, device=device, dtype=dtype)
+    qn = layer_ops.kv_norm_rope_append(kva, wn, pos, cache, bt, 1e-6, 10000.0, overlap=True, q_in=qa,
+                                       q_norm_weight=wq, q_eps=1e-6)
+    torch.cuda.synchronize()
+    _close(qn, F.rms_norm(qa.float(), (qr,), wq.float(), 1e-6), dtype)
+    rows = torch.arange(batch, device=device)
+    idx = (bt[rows, (pos // page).long()].long(), (pos % page).long())
+    _close(cache[idx][:, :r], F.rms_norm(kva[:, :r].float(), (r,), wn.float(), 1e-6), dtype)

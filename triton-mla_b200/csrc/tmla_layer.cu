@@ -231,12 +231,86 @@ __global__ void __launch_bounds__(128) q_absorb_rope_kernel(TmlaQPrepParams p) {
 
 // ---------------------------------------------------------------------------- kv: norm + RoPE + append
 // One warp per request.
+// dst[e] = src[e] * rsqrt(mean(src^2) + eps) * w[e] for e < n, by one warp.  16-bit rows
+// with 16-byte alignment and n <= 2048 take 16-byte loads, every lane issuing its loads of the
+// row and of the weight at once (at most 8 each); other rows go element by element.
+template <typename T>
+__device__ __forceinline__ void rms_norm_row(const T* src, const T* w, T* dst, int n, float eps, int lane) {
+  constexpr int kMaxVec = 8;
+  if constexpr (sizeof(T) == 2) {
+    if (n % 8 == 0 && n <= 8 * 32 * kMaxVec && ((uintptr_t)src % 16) == 0 && ((uintptr_t)w % 16) == 0 &&
+        ((uintptr_t)dst % 16) == 0) {
+      const int nvec = n / 8;
+      uint4 xv[kMaxVec], wv[kMaxVec];
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) {
+          xv[i] = reinterpret_cast<const uint4*>(src)[c];
+          wv[i] = reinterpret_cast<const uint4*>(w)[c];
+        }
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        if (lane + 32 * i < nvec) {
+          const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float a, b;
+            unpack2(xw[j], src, a, b);
+            ss = fmaf(a, a, fmaf(b, b, ss));
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss / (float)n + eps);
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) {
+          const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+          const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float xa, xb, wa, wb;
+            unpack2(xw[j], src, xa, xb);
+            unpack2(ww[j], src, wa, wb);
+            const T pr[2] = {cvt<T>(xa * rstd * wa), cvt<T>(xb * rstd * wb)};
+            ow[j] = *reinterpret_cast<const uint32_t*>(pr);
+          }
+          reinterpret_cast<uint4*>(dst)[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+      return;
+    }
+  }
+  float ss = 0.f;
+  for (int e = lane; e < n; e += 32) {
+    const float x = ld(src + e);
+    ss = fmaf(x, x, ss);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = rsqrtf(ss / (float)n + eps);
+  for (int e = lane; e < n; e += 32) dst[e] = cvt<T>(ld(src + e) * rstd * ld(w + e));
+}
+
+// Grid (ceil(batch / 4), 1 or 2), 128 threads, one warp per request.  blockIdx.y = 0: the
+// cache row (kv_norm, RoPE of k_pe, append); blockIdx.y = 1: the query path's q_norm.
 template <typename T>
 __global__ void __launch_bounds__(128) kv_append_kernel(TmlaKvAppendParams p) {
   after_predecessor();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x * 4 + warp;
   if (b >= p.batch) return;
+  if (blockIdx.y == 1) {
+    rms_norm_row(static_cast<const T*>(p.q_in) + (int64_t)b * p.q_in_stride_b, static_cast<const T*>(p.q_norm_weight),
+                 static_cast<T*>(p.q_out) + (int64_t)b * p.q_out_stride_b, p.q_rank, p.q_eps, lane);
+    return;
+  }
   const int R = p.rank, dr = p.d_rope, half = dr / 2;
   const T* src = static_cast<const T*>(p.kv_in) + (int64_t)b * p.kv_in_stride_b;
   const int pos = p.positions[b];
@@ -256,72 +330,7 @@ __global__ void __launch_bounds__(128) kv_append_kernel(TmlaKvAppendParams p) {
     return;
   }
   T* dst = static_cast<T*>(p.kv_cache) + page * p.kv_stride_page + slot * p.kv_stride_tok;
-  const T* wn = static_cast<const T*>(p.norm_weight);
-  // 16-bit rows with 16-byte alignment: every lane issues its 16-byte loads of the latent
-  // row and of the norm weight at once (at most 8 each, rank <= 2048), then normalises.
-  constexpr int kMaxVec = 8;
-  bool done = false;
-  if constexpr (sizeof(T) == 2) {
-    if (R % 8 == 0 && R <= 8 * 32 * kMaxVec && ((uintptr_t)src % 16) == 0 && ((uintptr_t)wn % 16) == 0 &&
-        ((uintptr_t)dst % 16) == 0) {
-      done = true;
-      const int nvec = R / 8;
-      uint4 xv[kMaxVec], wv[kMaxVec];
-#pragma unroll
-      for (int i = 0; i < kMaxVec; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nvec) {
-          xv[i] = reinterpret_cast<const uint4*>(src)[c];
-          wv[i] = reinterpret_cast<const uint4*>(wn)[c];
-        }
-      }
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < kMaxVec; ++i) {
-        if (lane + 32 * i < nvec) {
-          const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float a, b;
-            unpack2(xw[j], src, a, b);
-            ss = fmaf(a, a, fmaf(b, b, ss));
-          }
-        }
-      }
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rstd = rsqrtf(ss / (float)R + p.eps);
-#pragma unroll
-      for (int i = 0; i < kMaxVec; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nvec) {
-          const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-          const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
-          uint32_t ow[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float xa, xb, wa, wb;
-            unpack2(xw[j], src, xa, xb);
-            unpack2(ww[j], src, wa, wb);
-            const T pr[2] = {cvt<T>(xa * rstd * wa), cvt<T>(xb * rstd * wb)};
-            ow[j] = *reinterpret_cast<const uint32_t*>(pr);
-          }
-          reinterpret_cast<uint4*>(dst)[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-        }
-      }
-    }
-  }
-  if (!done) {
-    float ss = 0.f;
-    for (int e = lane; e < R; e += 32) {
-      const float x = ld(src + e);
-      ss = fmaf(x, x, ss);
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rstd = rsqrtf(ss / (float)R + p.eps);
-    for (int e = lane; e < R; e += 32) dst[e] = cvt<T>(ld(src + e) * rstd * ld(wn + e));
-  }
+  rms_norm_row(src, static_cast<const T*>(p.norm_weight), dst, R, p.eps, lane);
   for (int k = lane; k < half; k += 32) {
     float oa, ob;
     rope_pair(ld(src + R + k), ld(src + R + k + half), pos, k, dr, p.rope_theta, oa, ob);
@@ -647,7 +656,8 @@ int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream) {
   if (p->batch == 0) return TMLA_OK;
   if (!p->kv_in || !p->norm_weight || !p->positions || !p->kv_cache) return TMLA_ERR_INVALID_ARG;
   if (p->block_table && p->bt_width <= 0) return TMLA_ERR_INVALID_ARG;
-  const dim3 grid((p->batch + 3) / 4), block(128);
+  if (p->q_in && (!p->q_norm_weight || !p->q_out || p->q_rank <= 0)) return TMLA_ERR_INVALID_ARG;
+  const dim3 grid((p->batch + 3) / 4, p->q_in ? 2 : 1), block(128);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
   cudaError_t e;

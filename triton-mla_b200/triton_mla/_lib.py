@@ -148,6 +148,13 @@ class TmlaKvAppendParams(ctypes.Structure):
         ("eps", ctypes.c_float),
         ("rope_theta", ctypes.c_float),
         ("flags", ctypes.c_int32),
+        ("q_in", ctypes.c_void_p),
+        ("q_in_stride_b", ctypes.c_int64),
+        ("q_norm_weight", ctypes.c_void_p),
+        ("q_out", ctypes.c_void_p),
+        ("q_out_stride_b", ctypes.c_int64),
+        ("q_rank", ctypes.c_int32),
+        ("q_eps", ctypes.c_float),
     ]
 
 

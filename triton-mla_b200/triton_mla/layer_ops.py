@@ -56,9 +56,13 @@ def q_absorb_rope(q_in: torch.Tensor, w_kv_b: torch.Tensor, positions: torch.Ten
 
 def kv_norm_rope_append(kv_in: torch.Tensor, norm_weight: torch.Tensor, positions: torch.Tensor,
                         kv_cache: torch.Tensor, block_table, eps: float, rope_theta: float,
-                        seqlens_out: torch.Tensor | None = None, overlap: bool = False) -> None:
+                        seqlens_out: torch.Tensor | None = None, overlap: bool = False,
+                        q_in: torch.Tensor | None = None, q_norm_weight: torch.Tensor | None = None,
+                        q_eps: float = 1e-6):
     """Write ``[rmsnorm(kv_in[:, :rank]) | rope(kv_in[:, rank:])]`` at each request's position.
-    ``overlap`` as in ``q_absorb_rope`` (the preceding kernel must not write ``norm_weight``)."""
+    ``overlap`` as in ``q_absorb_rope`` (the preceding kernel must not write a norm weight).
+    With ``q_in`` [batch, q_rank] the same launch also returns ``rmsnorm(q_in) * q_norm_weight``
+    (contiguous); otherwise it returns None."""
     if kv_cache.dim() == 4:
         kv_cache = kv_cache.squeeze(2)
     batch, width = kv_in.shape
@@ -67,14 +71,22 @@ def kv_norm_rope_append(kv_in: torch.Tensor, norm_weight: torch.Tensor, position
     assert kv_cache.shape[-1] == width
     if block_table is not None:
         assert block_table.dtype == torch.int32 and block_table.stride(-1) == 1
+    q_out = None
+    if q_in is not None:
+        assert q_in.dim() == 2 and q_in.shape[0] == batch and q_in.stride(-1) == 1 and q_in.dtype == kv_in.dtype
+        assert q_norm_weight is not None and q_norm_weight.shape == (q_in.shape[1],)
+        q_out = torch.empty(q_in.shape, dtype=q_in.dtype, device=q_in.device)
     p = _lib.TmlaKvAppendParams(
         kv_in.data_ptr(), kv_in.stride(0), norm_weight.data_ptr(), positions.data_ptr(), _ptr(seqlens_out),
         kv_cache.data_ptr(), kv_cache.stride(0), kv_cache.stride(1), kv_cache.shape[0], kv_cache.shape[1],
         _ptr(block_table), 0 if block_table is None else block_table.stride(0),
         0 if block_table is None else block_table.shape[1], _status_word(kv_in.device).data_ptr(),
         batch, rank, width - rank, _DTYPE_CODES[kv_in.dtype], float(eps), float(rope_theta),
-        _lib.LAYER_FLAG_PDL if overlap else 0)
+        _lib.LAYER_FLAG_PDL if overlap else 0,
+        _ptr(q_in), 0 if q_in is None else q_in.stride(0), _ptr(q_norm_weight), _ptr(q_out),
+        0 if q_out is None else q_out.stride(0), 0 if q_in is None else q_in.shape[1], float(q_eps))
     _lib.check(_lib.load().tmla_kv_norm_rope_append(ctypes.byref(p), _stream(kv_in)), "tmla_kv_norm_rope_append")
+    return q_out
 
 
 def o_unabsorb(o: torch.Tensor, w_kv_b: torch.Tensor, d_nope: int, d_v: int, overlap: bool = False) -> torch.Tensor:

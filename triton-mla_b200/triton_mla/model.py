@@ -137,14 +137,16 @@ class MLA(nn.Module):
         cfg = self.cfg
         batch = x.shape[0]
         qa, kva = F.linear(x, self._w_a()).split([cfg.q_lora_rank, cfg.kv_cache_dim], dim=-1)
-        q = self.wq_b(self.q_norm(qa)).view(batch, cfg.num_heads, cfg.qk_head_dim)
         positions = cache_seqlens.to(torch.int32).contiguous()
         bt = None if block_table is None else block_table.to(torch.int32).contiguous()
         seqlens = torch.empty_like(positions)
         # The layer ops launch as programmatic dependents of the kernel before them (their
         # weight loads and launch overlap its end): none of those kernels writes a weight.
-        layer_ops.kv_norm_rope_append(kva, self.kv_norm.weight, positions, kv_cache, bt, self.kv_norm.eps,
-                                      cfg.rope_theta, seqlens_out=seqlens, overlap=True)
+        # One launch appends the cache row and applies q_norm to the other half of the GEMM.
+        qn = layer_ops.kv_norm_rope_append(kva, self.kv_norm.weight, positions, kv_cache, bt, self.kv_norm.eps,
+                                           cfg.rope_theta, seqlens_out=seqlens, overlap=True, q_in=qa,
+                                           q_norm_weight=self.q_norm.weight, q_eps=self.q_norm.eps)
+        q = self.wq_b(qn).view(batch, cfg.num_heads, cfg.qk_head_dim)
         q_full = layer_ops.q_absorb_rope(q, self.wkv_b.weight, positions, cfg.qk_nope_head_dim, cfg.v_head_dim,
                                          cfg.rope_theta, overlap=True)
         o = mla_decode(q_full, kv_cache, seqlens, bt, head_dim_v=cfg.kv_lora_rank, softmax_scale=self.softmax_scale,
