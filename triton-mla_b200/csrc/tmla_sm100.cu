@@ -364,6 +364,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t peer = rank ^ 1u;
   const int head_tile = blockIdx.x >> 1;
   const int h0 = head_tile * 128;
+  // Launched as a programmatic dependent: every global read (the plan, lengths, table, q,
+  // cache) and write comes after the preceding kernel has completed.
+  griddep_wait();
   // Which split of which request: the grid's (y, z) for uniform splits, or a plan entry.
   int split = blockIdx.y, b = blockIdx.z, nsplit = p.num_splits, slot = -1;
   if (args.units) {
@@ -1131,16 +1134,28 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   a.scale_log2 = p.softmax_scale * kLog2e;
   a.units = reinterpret_cast<const int4*>(units);
   const dim3 grid(2 * ((p.num_heads + 127) / 128), units ? 1 : p.num_splits, units ? num_units : p.batch);
+  // A programmatic dependent of the preceding kernel in the stream: the CTAs may be placed
+  // while that kernel finishes, and every read of an input follows griddep_wait().
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   cudaError_t e;
   if (p.dtype == TMLA_DTYPE_FP16) {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      mla_sm100_split_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
+      e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__half>, tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
   } else {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
     if (e == cudaSuccess)
-      mla_sm100_split_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
+      e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__nv_bfloat16>, tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
