@@ -487,6 +487,8 @@ def main(argv=None):
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "cutlass-mla"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "sm100", "generic"])
+    ap.add_argument("--q-len", type=int, default=1,
+                    help="query tokens per request (multi-token decode, e.g. speculative / MTP); 1 = the reference's")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (rank 0, N=1)")
     ap.add_argument("--clock-soak", type=float, default=0.6, help="seconds of untimed steps under the clock sampler")
     args = ap.parse_args(argv)
@@ -521,17 +523,25 @@ def main(argv=None):
     else:
         q, kv, lens, bt = make_workload(cfg, device, seed=1000 + rank)
     B = q.shape[0]
+    QL = max(1, args.q_len)
+    HR = 128 * QL  # query rows per request
     total_tokens = int(lens.sum())
+    # Rows attended: query token i of a request sees its first len - (QL - 1 - i) rows.
+    attended = sum(max(0, int(n) - (QL - 1 - i)) for n in lens.tolist() for i in range(QL))
+    if QL > 1:
+        g = torch.Generator(device=device).manual_seed(2000 + rank)
+        q = torch.randn(B, QL, 128, D_QK, generator=g, device=device, dtype=torch.bfloat16)
+    q3 = q.view(B, HR, D_QK)
     if not strong:
         job_tokens, job_batch = world * total_tokens, world * B
-    job_flops = decode_flops(job_tokens, 128)
-    flops = decode_flops(total_tokens, 128)
-    nbytes = decode_bytes(total_tokens, B, 128)
-    splits = get_num_splits(B, 128, int(lens.max()), torch.cuda.get_device_properties(device).multi_processor_count)
+    job_flops = decode_flops(job_tokens * attended / max(total_tokens, 1), 128)
+    flops = decode_flops(attended, 128)
+    nbytes = decode_bytes(total_tokens, B, HR)
+    splits = get_num_splits(B, HR, int(lens.max()), torch.cuda.get_device_properties(device).multi_processor_count)
     kname = selected_kernel(q, kv, bt, num_splits=splits, kernel=args.kernel)
     # A ragged batch follows a per-request split plan, made once outside the timed region
     # (it stays valid for any lengths of the batch); uniform batches use one split count.
-    plan = make_split_plan(lens, 128) if (cfg["ragged"] and kname == "sm100") else None
+    plan = make_split_plan(lens, HR) if (cfg["ragged"] and kname == "sm100") else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
@@ -576,22 +586,22 @@ def main(argv=None):
 
     # ---- dominant kernel alone (stage 1 through the C ABI), same stream, same flush discipline.
     lib = _lib.load()
-    lse = torch.empty(B, 128, dtype=torch.float32, device=device)
-    out = torch.empty(B, 128, D_V, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(B, HR, dtype=torch.float32, device=device)
+    out = torch.empty(B, HR, D_V, dtype=torch.bfloat16, device=device)
     if plan is None:
-        ws = torch.empty(max(lib.tmla_workspace_bytes(B, 128, max(splits, 2), D_V), 1), dtype=torch.uint8,
+        ws = torch.empty(max(lib.tmla_workspace_bytes(B, HR, max(splits, 2), D_V), 1), dtype=torch.uint8,
                          device=device)
-        o_bytes = (B * 128 * max(splits, 2) * D_V * 4 + 255) & ~255
+        o_bytes = (B * HR * max(splits, 2) * D_V * 4 + 255) & ~255
     else:
-        ws = torch.empty(max(lib.tmla_units_workspace_bytes(plan.num_slots, 128, D_V), 1), dtype=torch.uint8,
+        ws = torch.empty(max(lib.tmla_units_workspace_bytes(plan.num_slots, HR, D_V), 1), dtype=torch.uint8,
                          device=device)
-        o_bytes = (plan.num_slots * 128 * D_V * 4 + 255) & ~255
+        o_bytes = (plan.num_slots * HR * D_V * 4 + 255) & ~255
     p = _lib.TmlaDecodeParams(
-        q.data_ptr(), q.stride(0), q.stride(1), kv.data_ptr(), kv.stride(0), kv.stride(1), kv.shape[0], PAGE,
+        q3.data_ptr(), q3.stride(0), q3.stride(1), kv.data_ptr(), kv.stride(0), kv.stride(1), kv.shape[0], PAGE,
         lens.data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1], out.data_ptr(), out.stride(0), out.stride(1),
         lse.data_ptr(), lse.stride(0), ws.data_ptr(), ws.data_ptr() + o_bytes, _status_word(device).data_ptr(),
-        B, 128, D_QK, D_V, splits, _DTYPE_CODES[torch.bfloat16], _KERNELS[args.kernel],
-        0 if splits > 1 else _lib.FLAG_PARTIAL_ONLY, SCALE)
+        B, HR, D_QK, D_V, splits, _DTYPE_CODES[torch.bfloat16], _KERNELS[args.kernel],
+        0 if splits > 1 else _lib.FLAG_PARTIAL_ONLY, SCALE, QL)
     ks, ke = [], []
     for i in range(args.warmup + args.steps):
         flush.zero_()
@@ -620,8 +630,9 @@ def main(argv=None):
     lens_h = lens.cpu().pin_memory()
     bt_h = bt.cpu().pin_memory()
     nbuf = 2
-    out_h = [torch.empty(B, 128, D_V, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
-    lse_h = [torch.empty(B, 128, dtype=torch.float32).pin_memory() for _ in range(nbuf)]
+    o_shape = (B, QL, 128, D_V) if QL > 1 else (B, 128, D_V)
+    out_h = [torch.empty(o_shape, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    lse_h = [torch.empty(o_shape[:-1], dtype=torch.float32).pin_memory() for _ in range(nbuf)]
     h2d = q_h.numel() * 2 + lens_h.numel() * 4 + bt_h.numel() * 4
     d2h = out_h[0].numel() * 2 + lse_h[0].numel() * 4
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
@@ -729,7 +740,8 @@ def main(argv=None):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic N(0,1) (no dataset; BASELINE configs are synthetic)",
-        "config": {"workload": cfg["desc"], "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
+        "config": {"workload": cfg["desc"] + (f", {QL} query tokens per request (causal)" if QL > 1 else ""),
+                   "q_len": QL, "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
                    "page_size": PAGE, "tokens_per_job": job_tokens,
                    "tokens_per_gpu": total_tokens,
                    "num_splits": splits if plan is None else

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define TMLA_ABI_VERSION 1
+#define TMLA_ABI_VERSION 2
 
 /* Return codes. */
 #define TMLA_OK 0
@@ -61,7 +61,10 @@ extern "C" {
 #define TMLA_FLAG_PARTIAL_ONLY 0x1  /* write ws_o / ws_lse even when num_splits == 1 (stage-1 semantics) */
 
 typedef struct TmlaDecodeParams {
-  /* q [batch, num_heads, d_qk]: absorbed nope query (first d_v dims) then the RoPE query. */
+  /* q [batch, num_heads, d_qk]: absorbed nope query (first d_v dims) then the RoPE query.
+     With q_len > 1 (several new tokens per request, e.g. multi-token prediction) the
+     num_heads rows are q_len groups of num_heads / q_len heads, one group per token, and
+     row group i attends causally: to the first seqlens[b] - (q_len - 1 - i) cache rows. */
   const void* q;
   int64_t q_stride_b, q_stride_h;
 
@@ -95,6 +98,7 @@ typedef struct TmlaDecodeParams {
   int32_t kernel;                  /* TMLA_KERNEL_* */
   int32_t flags;                   /* TMLA_FLAG_* bits */
   float softmax_scale;
+  int32_t q_len;                   /* query tokens per request (0 or 1: one); divides num_heads */
 } TmlaDecodeParams;
 
 /* Whole decode: partial attention over num_splits KV ranges, then the merge.

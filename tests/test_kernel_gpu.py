@@ -544,3 +544,69 @@ def test_device_plan_and_decode_in_one_graph(device):
         _check_device_plan(new, plan)
         assert read_status(device) == 0
     del graph
+
+
+# ----------------------------------------------------------------------------- several query tokens
+# q [batch, q_len, heads, d] (an extension: the reference decodes one token per request).  Token i
+# of a request is its (len - q_len + i)-th row, so it attends to the first len - (q_len - 1 - i)
+# cache rows; the oracle runs each token as a one-token decode over that many rows.
+def _multi_token_ref(case, q4, seqlens):
+    q_len = q4.shape[1]
+    ref_out, ref_lse, per_token_lens = [], [], []
+    for i in range(q_len):
+        li = torch.clamp(seqlens - (q_len - 1 - i), min=0).to(torch.int32)
+        o, l = oracle_of(dict(case, q=q4[:, i].contiguous(), seqlens=li))
+        ref_out.append(o)
+        ref_lse.append(l)
+        per_token_lens.append(li.numpy())
+    return np.stack(ref_out, 1), np.stack(ref_lse, 1), np.stack(per_token_lens, 1)
+
+
+def _multi_token_case(lens, q_len, heads, seed):
+    case = recipes.paged_case(lens, q_len * heads, 64, seed=seed)
+    q4 = case["q"].view(len(lens), q_len, heads, case["q"].shape[-1])
+    return (case, q4) + _multi_token_ref(case, q4, case["seqlens"])
+
+
+@pytest.mark.parametrize("q_len,heads,kernel", [
+    (2, 128, "auto"), (3, 128, "auto"), (4, 128, "auto"), (2, 128, "generic"), (2, 16, "auto"), (3, 20, "auto"),
+])
+@pytest.mark.parametrize("num_splits", [None, 1, 3])
+def test_multi_token_decode_matches_reference(device, q_len, heads, kernel, num_splits):
+    lens = [4096, 1, 0, 700, 2, 65]
+    case, q4, ref_out, ref_lse, tok_lens = _multi_token_case(lens, q_len, heads, seed=q_len * 10 + heads)
+    c = to_dev(case, device)
+    out, lse = mla_decode(q4.to(device), c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          num_splits=num_splits, return_lse=True, kernel=kernel)
+    assert out.shape == (len(lens), q_len, heads, 512) and lse.shape == (len(lens), q_len, heads)
+    expect = "sm100" if (heads % 128 == 0 and kernel == "auto") else "generic"
+    assert selected_kernel(q4.to(device), c["kv"], c["block_table"], kernel=kernel) == expect
+    for i in range(q_len):
+        check(out[:, i], lse[:, i], ref_out[:, i], ref_lse[:, i], tok_lens[:, i])
+    assert read_status(device) == 0
+
+
+def test_multi_token_decode_in_a_graph(device):
+    """Two query tokens per request, captured with num_splits=None (a device-made plan) and
+    replayed with new lengths."""
+    lens0 = [3000, 64, 1, 9000]
+    case, q4, _, _, _ = _multi_token_case(lens0, 2, 128, seed=77)
+    c = to_dev(case, device)
+    q = q4.to(device)
+    lens = c["seqlens"].clone()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        mla_decode(q, c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True, num_splits=2)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        g_out, g_lse = mla_decode(q, c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True)
+    for new in (lens0, [9000, 2, 0, 65]):
+        lens.copy_(torch.tensor(new, dtype=torch.int32, device=device))
+        graph.replay()
+        torch.cuda.synchronize(device)
+        ref_out, ref_lse, tok_lens = _multi_token_ref(case, q4, torch.tensor(new, dtype=torch.int32))
+        for i in range(2):
+            check(g_out[:, i], g_lse[:, i], ref_out[:, i], ref_lse[:, i], tok_lens[:, i])
+    del graph

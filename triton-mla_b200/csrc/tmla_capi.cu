@@ -51,6 +51,7 @@ int validate(const TmlaDecodeParams* p) {
   if (p->dtype != TMLA_DTYPE_BF16 && p->dtype != TMLA_DTYPE_FP16 && p->dtype != TMLA_DTYPE_FP32)
     return TMLA_ERR_INVALID_ARG;
   if (p->page_size <= 0) return TMLA_ERR_INVALID_ARG;
+  if (p->q_len < 0 || (p->q_len > 1 && p->num_heads % p->q_len)) return TMLA_ERR_INVALID_ARG;
   if (p->batch == 0) return TMLA_OK;
   if (!p->q || !p->kv || !p->seqlens || !p->out) return TMLA_ERR_INVALID_ARG;
   if (p->block_table) {

@@ -73,6 +73,10 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
   }
   int start, end;
   split_range(len, p.num_splits, split, start, end);
+  // Several query tokens per request: head row hh belongs to token hh / (H / q_len), which
+  // attends to the first len - (q_len - 1 - token) rows.
+  const int q_len = p.q_len > 1 ? p.q_len : 1;
+  const int h_tok = H / q_len;
 
   const float qscale = p.softmax_scale * kLog2e;
   for (int i = tid; i < kGenHeads * D; i += kGenThreads) {
@@ -124,6 +128,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
     // Scores: thread -> head (tid >> 4), tokens (tid & 15) and (tid & 15) + 16.
     {
       const int h = tid >> 4;
+      const int row_end = min(end, len - (q_len - 1 - min(h0 + h, H - 1) / h_tok));
       const float* qr = q_s + h * Dq;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -131,7 +136,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
         const T* kr = k_s + r * Dk;
         float s = 0.f;
         for (int d = 0; d < D; ++d) s = fmaf(qr[d], ld_f<T>(kr + d), s);
-        p_s[h * kGenTok + r] = (t0 + r < end) ? s : -INFINITY;
+        p_s[h * kGenTok + r] = (t0 + r < row_end) ? s : -INFINITY;
       }
     }
     __syncthreads();
@@ -146,7 +151,8 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
       for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float m_old = m_s[h];
       const float m_new = fmaxf(m_old, mx);
-      const float p0 = exp2f(s0 - m_new), p1 = exp2f(s1 - m_new);
+      const bool none = m_new == -INFINITY;  // every token so far masked for this row
+      const float p0 = none ? 0.f : exp2f(s0 - m_new), p1 = none ? 0.f : exp2f(s1 - m_new);
       float sum = p0 + p1;
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -154,7 +160,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
       p_s[h * kGenTok + r + 16] = p1;
       __syncwarp();
       if (r == 0) {
-        const float alpha = exp2f(m_old - m_new);
+        const float alpha = none ? 1.f : exp2f(m_old - m_new);
         a_s[h] = alpha;
         l_s[h] = l_s[h] * alpha + sum;
         m_s[h] = m_new;

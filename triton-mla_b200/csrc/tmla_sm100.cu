@@ -388,8 +388,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) TMLA_SPAN(0);
   // The request length, the block-table entries of the split and this CTA's Q rows are
   // requested before the set-up below, so that their latency overlaps it.
-  const int len_in = __ldg(p.seqlens + b);
+  const int len_req = __ldg(p.seqlens + b);
   const int cap = p.block_table ? p.bt_width * p.page_size : p.page_size;
+  // Several query tokens per request: this head tile's token attends causally, to the
+  // request's first len - (q_len - 1 - token) rows (a length out of range is flagged below).
+  int len_in = len_req;
+  if (p.q_len > 1 && len_req >= 0 && len_req <= cap)
+    len_in = max(0, len_req - (p.q_len - 1 - h0 / (H / p.q_len)));
   const int g = args.rows_per_load;  // token rows per TMA box
   const int nsub = kTile / g;
   // The producer reads the page ids of its first tile as if the request filled its table:
@@ -1094,6 +1099,7 @@ int sm100_supported(const TmlaDecodeParams& p) {
   if (p.q_stride_b % 8 || p.q_stride_h % 8 || p.kv_stride_page % 8 || p.kv_stride_tok % 8) return 0;
   if ((uintptr_t)p.out % 16 || p.out_stride_b % 8 || p.out_stride_h % 8) return 0;
   if (p.block_table && sm100::pow2_rows(p.page_size) < 8) return 0;
+  if (p.q_len > 1 && (p.num_heads / p.q_len) % 128) return 0;  // a head tile within one query token
   return 1;
 }
 

@@ -15,7 +15,7 @@ from pathlib import Path
 LIB_NAME = "libtriton_mla_b200.so"
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 OK = 0
 ERR_INVALID_ARG = 1
@@ -96,6 +96,7 @@ class TmlaDecodeParams(ctypes.Structure):
         ("kernel", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float),
+        ("q_len", ctypes.c_int32),
     ]
 
 

@@ -222,7 +222,11 @@ def mla_decode(
 
     Args:
         q: [batch, num_heads, head_dim_v + rope_dim]; the first head_dim_v dims
-            are the W_UK-absorbed nope query, the rest the RoPE query.
+            are the W_UK-absorbed nope query, the rest the RoPE query.  Extension: a 4-D
+            q [batch, q_len, num_heads, d] holds q_len new tokens per request (the last q_len
+            of its cache_seqlens rows, e.g. multi-token prediction); token i attends causally
+            to the first cache_seqlens - (q_len - 1 - i) rows, and out / lse gain the same
+            q_len axis.
         kv_cache: paged [num_blocks, page_size, D] when block_table is given,
             otherwise contiguous [batch, max_seqlen, D]; [..., 1, D] accepted.
         cache_seqlens: [batch] number of valid tokens per sequence.
@@ -241,6 +245,17 @@ def mla_decode(
     Returns:
         out [batch, num_heads, head_dim_v] (and lse [batch, num_heads] fp32).
     """
+    q_len, q4 = 1, None
+    if q.dim() == 4:
+        q4 = q.shape
+        q_len = q4[1]
+        assert q_len >= 1 and q.stride(-1) == 1
+        if q.stride(1) != q4[2] * q.stride(2):
+            q = q.contiguous()
+        q = q.view(q4[0], q_len * q4[2], q4[3])
+        if out is not None:
+            assert out.dim() == 4 and out.shape[:3] == q4[:3]
+            out = out.view(q4[0], q_len * q4[2], out.shape[3])
     if kv_cache.dim() == 4:
         assert kv_cache.shape[2] == 1, "MLA uses a single shared latent KV head"
         kv_cache = kv_cache.squeeze(2)
@@ -292,7 +307,7 @@ def mla_decode(
             # from the lengths at replay time; the generic kernel's split count is sized for
             # the longest request the cache holds.
             if kernel != "generic" and selected_kernel(q, kv_cache, block_table, head_dim_v, num_splits=1,
-                                                       kernel=kernel) == "sm100":
+                                                       kernel=kernel, q_len=q_len) == "sm100":
                 plan = make_device_split_plan(cache_seqlens, num_heads)
                 num_splits = 1
             else:
@@ -302,7 +317,7 @@ def mla_decode(
             # The one host sync (the reference reads max(cache_seqlens) here, kernel.py:264-266).
             lens_host = cache_seqlens.cpu()
             if kernel != "generic" and selected_kernel(q, kv_cache, block_table, head_dim_v, num_splits=1,
-                                                       kernel=kernel) == "sm100":
+                                                       kernel=kernel, q_len=q_len) == "sm100":
                 # The tcgen05 kernel takes a split count per request: the planner's choice.
                 units, req_first = plan_units(lens_host.numpy(), num_heads, _num_sms(device))
                 counts = units[:, 2]
@@ -323,8 +338,15 @@ def mla_decode(
     else:
         assert out.shape == (batch, num_heads, head_dim_v) and out.dtype == q.dtype and out.stride(-1) == 1
     lse = torch.empty(batch, num_heads, dtype=torch.float32, device=device)
+
+    def _shaped(o, l):
+        if q4 is not None:
+            o = o.view(q4[0], q_len, q4[2], o.shape[-1])
+            l = l.view(q4[0], q_len, q4[2])
+        return (o, l) if return_lse else o
+
     if batch == 0:
-        return (out, lse) if return_lse else out
+        return _shaped(out, lse)
 
     lib = _lib.load()
     if plan is not None:
@@ -348,7 +370,7 @@ def mla_decode(
         lse.data_ptr(), lse.stride(0),
         ws_o, ws_lse, _status_word(device).data_ptr(),
         batch, num_heads, d_qk, head_dim_v, num_splits,
-        _DTYPE_CODES[q.dtype], _KERNELS[kernel], 0, float(softmax_scale),
+        _DTYPE_CODES[q.dtype], _KERNELS[kernel], 0, float(softmax_scale), q_len,
     )
     prev = torch.cuda.current_device()
     if prev != device.index:
@@ -368,15 +390,16 @@ def mla_decode(
         st = read_status(device)
         if st:
             raise RuntimeError(f"mla_decode device status 0x{st:x} (bad page id / length, or a wait timed out)")
-    if return_lse:
-        return out, lse
-    return out
+    return _shaped(out, lse)
 
 
-def selected_kernel(q, kv_cache, block_table=None, head_dim_v=512, num_splits=1, kernel="auto") -> str:
+def selected_kernel(q, kv_cache, block_table=None, head_dim_v=512, num_splits=1, kernel="auto", q_len=1) -> str:
     """Which kernel ``mla_decode`` runs for these tensors: "sm100" or "generic"."""
     if kv_cache.dim() == 4:
         kv_cache = kv_cache.squeeze(2)
+    if q.dim() == 4:
+        q_len = q.shape[1]
+        q = q.reshape(q.shape[0], q.shape[1] * q.shape[2], q.shape[3])
     batch, num_heads, d_qk = q.shape
     p = _lib.TmlaDecodeParams()
     p.q, p.q_stride_b, p.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
@@ -390,7 +413,7 @@ def selected_kernel(q, kv_cache, block_table=None, head_dim_v=512, num_splits=1,
     p.seqlens = p.out = p.ws_o = p.ws_lse = 256  # only checked for being non-null and aligned
     p.out_stride_b, p.out_stride_h = num_heads * head_dim_v, head_dim_v
     p.batch, p.num_heads, p.d_qk, p.d_v, p.num_splits = batch, num_heads, d_qk, head_dim_v, num_splits
-    p.dtype, p.kernel = _DTYPE_CODES[q.dtype], _KERNELS[kernel]
+    p.dtype, p.kernel, p.q_len = _DTYPE_CODES[q.dtype], _KERNELS[kernel], int(q_len)
     k = _lib.load().tmla_select_kernel(ctypes.byref(p))
     if k < 0:
         raise _lib.LibraryError(-k, "tmla_select_kernel")
