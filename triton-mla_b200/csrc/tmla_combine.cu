@@ -5,7 +5,8 @@
 // gives out 0 and lse -inf, the final LSE is converted to natural log), but
 // warps over (request, head, 128-column group) with 16-byte loads of the fp32
 // partials, 8 splits in flight, instead of one 4-warp program per row with a
-// serial split loop.
+// serial split loop.  For d_v = 512 and at most 4 splits, one warp per row with
+// every load of the row in flight (fewer, fuller warps: one wave of CTAs).
 #include "tmla_common.cuh"
 #include "tmla_ptx.cuh"
 
@@ -105,6 +106,78 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
   T* dst = out + (int64_t)b * osb + (int64_t)h * osh + grp * 128 + 4 * lane;
   store4<T>(dst, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
   if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+}
+
+// One warp merges one output row of d_v = 512 (the DeepSeek shape): lane l owns the float4
+// columns l, l + 32, l + 64 and l + 96, and two splits are in flight at a time (eight 16-byte
+// loads per lane, issued with the LSE loads before the weights are known).  Split s of the row
+// is at O + s * split_f4 float4s and its base-2 LSE at L[s * lse_stride].
+template <typename T>
+__device__ __forceinline__ void merge_row512(const float* __restrict__ O, int64_t split_f4, const float* __restrict__ L,
+                                             int64_t lse_stride, int S, T* dst, float* lse_dst, int lane) {
+  const float4* src = reinterpret_cast<const float4*>(O) + lane;
+  float4 v[2][4];
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      v[u][c] = u < S ? __ldg(src + u * split_f4 + 32 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float l0 = lane < S ? L[lane * lse_stride] : -INFINITY;
+  const float l1 = lane + 32 < S ? L[(lane + 32) * lse_stride] : -INFINITY;
+  float m = fmaxf(l0, l1);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (m == -INFINITY) m = 0.f;
+  const float w0 = exp2f(l0 - m), w1 = exp2f(l1 - m);  // 0 for -inf (empty splits, lanes past S)
+  float wsum = w0 + w1;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+  float4 acc[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < S; s0 += 2) {
+    if (s0 > 0) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          v[u][c] = s0 + u < S ? __ldg(src + (s0 + u) * split_f4 + 32 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int s = s0 + u;
+      const float w = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);  // 0 past S (l = -inf)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        acc[c].x = fmaf(w, v[u][c].x, acc[c].x);
+        acc[c].y = fmaf(w, v[u][c].y, acc[c].y);
+        acc[c].z = fmaf(w, v[u][c].z, acc[c].z);
+        acc[c].w = fmaf(w, v[u][c].w, acc[c].w);
+      }
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    store4<T>(dst + 4 * (lane + 32 * c), make_float4(acc[c].x * inv, acc[c].y * inv, acc[c].z * inv, acc[c].w * inv));
+  if (lse_dst && lane == 0) *lse_dst = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+}
+
+constexpr int kRowWarps = 4;  // rows per CTA of the d_v = 512 merges (8 CTAs, 1024 threads per SM)
+
+// Uniform splits, d_v = 512: ws_o [B, H, S, 512], ws_lse [B, H, S]; one warp per (b, h).
+template <typename T>
+__global__ void __launch_bounds__(kRowWarps * 32, 8)
+    mla_combine_row512_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
+                              int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();  // a programmatic successor may be scheduled now
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * H) return;
+  const int b = (int)(row / H), h = (int)(row - (int64_t)b * H);
+  merge_row512<T>(ws_o + row * S * 512, 128, ws_lse + row * S, 1, S, out + (int64_t)b * osb + (int64_t)h * osh,
+                  lse ? lse + (int64_t)b * lsb + h : nullptr, lane);
 }
 
 // Merge of a per-request split plan (tmla_decode_units): request b's partials sit in slots
@@ -218,7 +291,13 @@ static int launch_combine_t(const float* ws_o, const float* ws_lse, void* out, i
   cfg.numAttrs = 1;
   T* o = static_cast<T*>(out);
   cudaError_t e;
-  if (vec_ok) {
+  // d_v = 512 with few splits: a warp per row, all of a row's loads in flight at once.  With
+  // many splits (long requests, few rows) four warps per row over 8 splits at a time do better.
+  if (vec_ok && DV == 512 && S <= 4) {
+    cfg.blockDim = dim3(kRowWarps * 32);
+    cfg.gridDim = dim3((unsigned)((rows + kRowWarps - 1) / kRowWarps));
+    e = cudaLaunchKernelEx(&cfg, mla_combine_row512_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S);
+  } else if (vec_ok) {
     const int64_t warps = rows * (DV / 128);
     cfg.gridDim = dim3((unsigned)((warps + kCombineWarps - 1) / kCombineWarps));
     e = cudaLaunchKernelEx(&cfg, mla_combine_vec_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
