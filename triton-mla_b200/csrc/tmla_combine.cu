@@ -52,7 +52,7 @@ __device__ __forceinline__ float cvt1<float>(float v) { return v; }
 // loads of 8 splits are issued before their FMAs, so a row costs S/8 memory round
 // trips instead of S.
 template <typename T>
-__global__ void __launch_bounds__(kCombineWarps * 32)
+__global__ void __launch_bounds__(kCombineWarps * 32, 4)
     mla_combine_vec_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
                            int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S,
                            int DV) {
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, 8)
 // with no slots (one split) was written by the split kernel and is skipped.  Same layout of
 // the work and the same arithmetic as mla_combine_vec_kernel.
 template <typename T>
-__global__ void __launch_bounds__(kCombineWarps * 32)
+__global__ void __launch_bounds__(kCombineWarps * 32, 4)
     mla_combine_slots_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
                              const int32_t* __restrict__ req_first, T* __restrict__ out, int64_t osb, int64_t osh,
                              float* __restrict__ lse, int64_t lsb, int B, int H, int DV) {
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
 
 // General path (any d_v, any split count): one warp per row, serial over splits.
 template <typename T>
-__global__ void __launch_bounds__(kCombineWarps * 32)
+__global__ void __launch_bounds__(kCombineWarps * 32, 4)
     mla_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
                        int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S, int DV) {
   ptx::griddep_wait();
