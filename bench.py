@@ -64,9 +64,11 @@ def decode_flops(total_tokens, heads):
     return float(total_tokens) * heads * 2 * (D_QK + D_V)
 
 
-def decode_bytes(total_tokens, batch, heads, elt=2):
-    """Algorithmic bytes of one call: cache rows + q + out (bench.py:80 of the reference)."""
-    return float(total_tokens * D_QK + batch * heads * D_QK + batch * heads * D_V) * elt
+def decode_bytes(total_tokens, batch, heads, elt=2, row_bytes=None):
+    """Algorithmic bytes of one call: cache rows + q + out (bench.py:80 of the reference);
+    ``row_bytes`` overrides the cache bytes per token (656 for FP8 rows)."""
+    rows = total_tokens * (row_bytes if row_bytes else D_QK * elt)
+    return float(rows + (batch * heads * D_QK + batch * heads * D_V) * elt)
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant kernel,
@@ -487,6 +489,8 @@ def main(argv=None):
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "cutlass-mla"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "sm100", "generic"])
+    ap.add_argument("--kv-fp8", action="store_true",
+                    help="an FP8 cache (656-byte rows, triton_mla.fp8_cache; CUDA-core kernel)")
     ap.add_argument("--q-len", type=int, default=1,
                     help="query tokens per request (multi-token decode, e.g. speculative / MTP); 1 = the reference's")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (rank 0, N=1)")
@@ -532,11 +536,14 @@ def main(argv=None):
         g = torch.Generator(device=device).manual_seed(2000 + rank)
         q = torch.randn(B, QL, 128, D_QK, generator=g, device=device, dtype=torch.bfloat16)
     q3 = q.view(B, HR, D_QK)
+    if args.kv_fp8:
+        from triton_mla import fp8_cache
+        kv = fp8_cache.quantize_kv(kv)
     if not strong:
         job_tokens, job_batch = world * total_tokens, world * B
     job_flops = decode_flops(job_tokens * attended / max(total_tokens, 1), 128)
     flops = decode_flops(attended, 128)
-    nbytes = decode_bytes(total_tokens, B, HR)
+    nbytes = decode_bytes(total_tokens, B, HR, row_bytes=656 if args.kv_fp8 else None)
     splits = get_num_splits(B, HR, int(lens.max()), torch.cuda.get_device_properties(device).multi_processor_count)
     kname = selected_kernel(q, kv, bt, num_splits=splits, kernel=args.kernel)
     # A ragged batch follows a per-request split plan, made once outside the timed region
@@ -601,7 +608,8 @@ def main(argv=None):
         lens.data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1], out.data_ptr(), out.stride(0), out.stride(1),
         lse.data_ptr(), lse.stride(0), ws.data_ptr(), ws.data_ptr() + o_bytes, _status_word(device).data_ptr(),
         B, HR, D_QK, D_V, splits, _DTYPE_CODES[torch.bfloat16], _KERNELS[args.kernel],
-        0 if splits > 1 else _lib.FLAG_PARTIAL_ONLY, SCALE, QL)
+        0 if splits > 1 else _lib.FLAG_PARTIAL_ONLY, SCALE, QL,
+        _lib.KV_FP8_E4M3 if args.kv_fp8 else _lib.KV_SAME)
     ks, ke = [], []
     for i in range(args.warmup + args.steps):
         flush.zero_()
@@ -740,8 +748,9 @@ def main(argv=None):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic N(0,1) (no dataset; BASELINE configs are synthetic)",
-        "config": {"workload": cfg["desc"] + (f", {QL} query tokens per request (causal)" if QL > 1 else ""),
-                   "q_len": QL, "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
+        "config": {"workload": cfg["desc"] + (f", {QL} query tokens per request (causal)" if QL > 1 else "")
+                   + (", FP8 cache rows (656 B per token)" if args.kv_fp8 else ""),
+                   "q_len": QL, "kv_cache": "fp8_e4m3_656" if args.kv_fp8 else "bf16", "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
                    "page_size": PAGE, "tokens_per_job": job_tokens,
                    "tokens_per_gpu": total_tokens,
                    "num_splits": splits if plan is None else

@@ -60,6 +60,16 @@ extern "C" {
 /* Flags. */
 #define TMLA_FLAG_PARTIAL_ONLY 0x1  /* write ws_o / ws_lse even when num_splits == 1 (stage-1 semantics) */
 
+/* Cache row formats (TmlaDecodeParams.kv_format).
+   TMLA_KV_SAME: d_qk values of the q dtype per token.
+   TMLA_KV_FP8_E4M3: 656 bytes per token (d_qk 576, d_v 512): 512 float8 e4m3 latent values,
+   4 fp32 scales (scale i multiplies latent values 128 i .. 128 i + 127), then the 64 RoPE
+   values in bf16.  The kv strides count bytes.  q and out are bf16 or fp16; the CUDA-core
+   kernel runs it.  The reference has no FP8 cache; the layout is the public 656-byte FP8 MLA
+   cache row of FlashMLA (DeepSeek-V3.2). */
+#define TMLA_KV_SAME 0
+#define TMLA_KV_FP8_E4M3 1
+
 typedef struct TmlaDecodeParams {
   /* q [batch, num_heads, d_qk]: absorbed nope query (first d_v dims) then the RoPE query.
      With q_len > 1 (several new tokens per request, e.g. multi-token prediction) the
@@ -99,6 +109,7 @@ typedef struct TmlaDecodeParams {
   int32_t flags;                   /* TMLA_FLAG_* bits */
   float softmax_scale;
   int32_t q_len;                   /* query tokens per request (0 or 1: one); divides num_heads */
+  int32_t kv_format;               /* TMLA_KV_*: the cache row format */
 } TmlaDecodeParams;
 
 /* Whole decode: partial attention over num_splits KV ranges, then the merge.

@@ -610,3 +610,46 @@ def test_multi_token_decode_in_a_graph(device):
         for i in range(2):
             check(g_out[:, i], g_lse[:, i], ref_out[:, i], ref_lse[:, i], tok_lens[:, i])
     del graph
+
+
+# ----------------------------------------------------------------------------- FP8 cache rows
+# A uint8 cache of 656-byte rows (triton_mla.fp8_cache; an extension).  The oracle attends to
+# the dequantised rows, so the comparison measures the kernel, not the quantisation.
+@pytest.mark.parametrize("paged", [True, False])
+@pytest.mark.parametrize("num_splits", [None, 1, 3])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fp8_cache_matches_reference(device, paged, num_splits, dtype):
+    from triton_mla import fp8_cache
+    lens = [1000, 0, 77, 2048, 1]
+    if paged:
+        case = recipes.paged_case(lens, 128, 64, seed=91, dtype=dtype)
+    else:
+        g = torch.Generator().manual_seed(91)
+        case = dict(q=torch.randn(len(lens), 128, 576, generator=g).to(dtype),
+                    kv=torch.randn(len(lens), 2048, 576, generator=g).to(dtype),
+                    seqlens=torch.tensor(lens, dtype=torch.int32), block_table=None, scale=recipes.SCALE_192)
+    rows = fp8_cache.quantize_kv(case["kv"])
+    ref_case = dict(case, kv=fp8_cache.dequantize_kv(rows))
+    ref_out, ref_lse = oracle_of(ref_case)
+    c = to_dev(dict(case, kv=rows), device)
+    assert selected_kernel(c["q"], c["kv"], c["block_table"]) == "generic"
+    out, lse = mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          num_splits=num_splits, return_lse=True)
+    check(out, lse, ref_out, ref_lse, lens)
+    assert read_status(device) == 0
+
+
+def test_fp8_cache_with_several_query_tokens(device):
+    from triton_mla import fp8_cache
+    lens = [700, 3, 1500]
+    case, q4, _, _, _ = _multi_token_case(lens, 2, 128, seed=5)
+    rows = fp8_cache.quantize_kv(case["kv"])
+    ref_case = dict(case, kv=fp8_cache.dequantize_kv(rows))
+    ref_out, ref_lse, tok_lens = _multi_token_ref(ref_case, q4, case["seqlens"])
+    c = to_dev(dict(case, kv=rows), device)
+    out, lse = mla_decode(q4.to(device), c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          return_lse=True)
+    for i in range(2):
+        check(out[:, i], lse[:, i], ref_out[:, i], ref_lse[:, i], tok_lens[:, i])
+    with pytest.raises(_lib.LibraryError):
+        mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], kernel="sm100")

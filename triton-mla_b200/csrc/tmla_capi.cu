@@ -52,6 +52,9 @@ int validate(const TmlaDecodeParams* p) {
     return TMLA_ERR_INVALID_ARG;
   if (p->page_size <= 0) return TMLA_ERR_INVALID_ARG;
   if (p->q_len < 0 || (p->q_len > 1 && p->num_heads % p->q_len)) return TMLA_ERR_INVALID_ARG;
+  if (p->kv_format != TMLA_KV_SAME && p->kv_format != TMLA_KV_FP8_E4M3) return TMLA_ERR_INVALID_ARG;
+  if (p->kv_format == TMLA_KV_FP8_E4M3 && (p->d_qk != 576 || p->d_v != 512 || p->dtype == TMLA_DTYPE_FP32))
+    return TMLA_ERR_INVALID_ARG;
   if (p->batch == 0) return TMLA_OK;
   if (!p->q || !p->kv || !p->seqlens || !p->out) return TMLA_ERR_INVALID_ARG;
   if (p->block_table) {

@@ -13,6 +13,10 @@
 // accumulates P.V into registers (each thread owns up to 4 latent columns for
 // all 16 heads).  Output: the normalised partial and its base-2 LSE per split,
 // or, with one split, the final output and natural-log LSE directly.
+#include <cuda_fp8.h>
+
+#include <type_traits>
+
 #include "tmla_common.cuh"
 
 namespace tmla {
@@ -49,7 +53,37 @@ size_t generic_smem_bytes(int d_qk, int elt) {
   return f * 4 + (size_t)kGenTok * gen_row_pad(d_qk) * elt + 16;
 }
 
+// FP8 cache rows (TMLA_KV_FP8_E4M3, 656 bytes): the row of token t of request b, or nullptr
+// (flagged) when its block-table entry is outside the pool.
+__device__ __forceinline__ const unsigned char* fp8_row(const TmlaDecodeParams& p, int b, int t) {
+  const unsigned char* base = static_cast<const unsigned char*>(p.kv);
+  if (p.block_table == nullptr) return base + (int64_t)b * p.kv_stride_page + (int64_t)t * p.kv_stride_tok;
+  const int slot = t / p.page_size;
+  const int page = (slot < p.bt_width) ? p.block_table[(int64_t)b * p.bt_stride + slot] : -1;
+  if (page < 0 || (int64_t)page >= p.num_pages) {
+    if (p.status) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
+    return nullptr;
+  }
+  return base + (int64_t)page * p.kv_stride_page + (int64_t)(t - slot * p.page_size) * p.kv_stride_tok;
+}
+
+// Eight e4m3 values (one 8-byte word) times `scale`, as T.
 template <typename T>
+__device__ __forceinline__ void fp8x8_to(T* dst, uint2 w, float scale) {
+  const uint32_t words[2] = {w.x, w.y};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[i] >> (16 * j)), __NV_E4M3);
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+      dst[4 * i + 2 * j] = Elem<T>::from_f(f.x * scale);
+      dst[4 * i + 2 * j + 1] = Elem<T>::from_f(f.y * scale);
+    }
+  }
+}
+
+template <typename T, bool kFp8Cache>
 __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDecodeParams p, int vec_ok) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int D = p.d_qk, DV = p.d_v, H = p.num_heads;
@@ -99,7 +133,29 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
   constexpr int VE = Vec<T>::kPerChunk;
   for (int t0 = start; t0 < end; t0 += kGenTok) {
     // Stage the tile's cache rows (zeros past `end` or behind a bad page id).
-    if (vec_ok) {
+    if constexpr (kFp8Cache) {
+      // 656-byte rows: 64 words of 8 latent e4m3 values (scaled by the row's 4 fp32 scales)
+      // and 8 chunks of 8 bf16 RoPE values per token, dequantised into the tile as T.
+      for (int c = tid; c < kGenTok * 72; c += kGenThreads) {
+        const int r = c / 72, k = c - r * 72, tok = t0 + r;
+        const unsigned char* row = tok < end ? fp8_row(p, b, tok) : nullptr;
+        T* dst = k_s + r * Dk;
+        if (k < 64) {
+          if (row) {
+            const float scale = reinterpret_cast<const float*>(row + 512)[k >> 4];
+            fp8x8_to<T>(dst + 8 * k, *reinterpret_cast<const uint2*>(row + 8 * k), scale);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[8 * k + i] = st_f<T>(0.f);
+          }
+        } else {
+          const int e = 8 * (k - 64);
+          const __nv_bfloat16* rope = row ? reinterpret_cast<const __nv_bfloat16*>(row + 528) : nullptr;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dst[512 + e + i] = rope ? Elem<T>::from_f(__bfloat162float(rope[e + i])) : st_f<T>(0.f);
+        }
+      }
+    } else if (vec_ok) {
       const int chunks = D / VE;
       for (int c = tid; c < kGenTok * chunks; c += kGenThreads) {
         int r = c / chunks, e = (c - r * chunks) * VE;
@@ -228,14 +284,26 @@ static int launch_generic_t(const TmlaDecodeParams& p, cudaStream_t stream) {
   const int elt = (int)sizeof(T);
   const size_t smem = generic_smem_bytes(p.d_qk, elt);
   if (smem > 227 * 1024) return TMLA_ERR_UNSUPPORTED;
-  cudaError_t e = cudaFuncSetAttribute(mla_generic_split_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(mla_generic_split_kernel<T, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return -(int)e;
   const int VE = Vec<T>::kPerChunk;
   int vec_ok = (p.d_qk % VE == 0) && (p.kv_stride_tok % VE == 0) && (p.kv_stride_page % VE == 0) &&
                (((uintptr_t)p.kv) % 16 == 0);
   dim3 grid((p.num_heads + kGenHeads - 1) / kGenHeads, p.num_splits, p.batch);
-  mla_generic_split_kernel<T><<<grid, kGenThreads, smem, stream>>>(p, vec_ok);
+  if constexpr (!std::is_same<T, float>::value) {
+    if (p.kv_format == TMLA_KV_FP8_E4M3) {
+      // 8- and 16-byte loads from the rows: the base and the strides are 16-byte aligned.
+      if (((uintptr_t)p.kv) % 16 || p.kv_stride_tok % 16 || p.kv_stride_page % 16) return TMLA_ERR_MISALIGNED;
+      e = cudaFuncSetAttribute(mla_generic_split_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem);
+      if (e != cudaSuccess) return -(int)e;
+      mla_generic_split_kernel<T, true><<<grid, kGenThreads, smem, stream>>>(p, 0);
+      e = cudaGetLastError();
+      return e == cudaSuccess ? 0 : -(int)e;
+    }
+  }
+  mla_generic_split_kernel<T, false><<<grid, kGenThreads, smem, stream>>>(p, vec_ok);
   e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
 }

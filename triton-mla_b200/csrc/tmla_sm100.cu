@@ -1092,7 +1092,7 @@ static int pow2_rows(int page) {
 }  // namespace sm100
 
 int sm100_supported(const TmlaDecodeParams& p) {
-  if (p.d_qk != 576 || p.d_v != 512) return 0;
+  if (p.d_qk != 576 || p.d_v != 512 || p.kv_format != TMLA_KV_SAME) return 0;
   if (p.dtype != TMLA_DTYPE_BF16 && p.dtype != TMLA_DTYPE_FP16) return 0;
   if (p.batch > 65535 || p.num_splits > 65535) return 0;
   if (((uintptr_t)p.q | (uintptr_t)p.kv) % 16) return 0;

@@ -5,7 +5,7 @@ Exports the same names as the reference package (src/triton_mla/__init__.py:1-14
 ``libtriton_mla_b200.so``; there is no Triton and no CPU implementation.
 """
 
-from . import layer_ops, sharding
+from . import fp8_cache, layer_ops, sharding
 from .kernel import (SplitPlan, get_num_splits, make_device_split_plan, make_split_plan, mla_decode, read_status,
                      selected_kernel)
 from .model import MLA, MLAConfig, MLADecodeGraph

@@ -24,6 +24,8 @@ ERR_MISALIGNED = 3
 ERR_CUDA = 4
 ERR_WORKSPACE = 5
 LAYER_FLAG_PDL = 1
+KV_SAME = 0
+KV_FP8_E4M3 = 1
 
 STATUS_BAD_PAGE = 0x1
 STATUS_TIMEOUT = 0x2
@@ -97,6 +99,7 @@ class TmlaDecodeParams(ctypes.Structure):
         ("flags", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float),
         ("q_len", ctypes.c_int32),
+        ("kv_format", ctypes.c_int32),
     ]
 
 

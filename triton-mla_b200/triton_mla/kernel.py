@@ -35,6 +35,7 @@ _DTYPE_CODES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16,
 _KERNELS = {"auto": _lib.KERNEL_AUTO, "generic": _lib.KERNEL_GENERIC, "sm100": _lib.KERNEL_SM100}
 
 B200_NUM_SMS = 148
+FP8_ROW_BYTES = 656  # an FP8 cache row: 512 e4m3 latent values, 4 fp32 scales, 64 bf16 RoPE values
 
 
 def _is_pow2(v: int) -> bool:
@@ -262,11 +263,18 @@ def mla_decode(
     assert q.dim() == 3 and kv_cache.dim() == 3
     batch, num_heads, d_qk = q.shape
     d_rope = d_qk - head_dim_v
-    assert kv_cache.shape[-1] == d_qk
+    # Extension: a uint8 cache of FP8 rows (``fp8_cache``: 656 bytes per token, DeepSeek dims).
+    kv_format = _lib.KV_FP8_E4M3 if kv_cache.dtype == torch.uint8 else _lib.KV_SAME
+    if kv_format == _lib.KV_FP8_E4M3:
+        assert kv_cache.shape[-1] == FP8_ROW_BYTES and d_qk == 576 and head_dim_v == 512
+        assert q.dtype in (torch.bfloat16, torch.float16)
+    else:
+        assert kv_cache.shape[-1] == d_qk
     assert q.stride(-1) == 1 and kv_cache.stride(-1) == 1
     assert _is_pow2(head_dim_v)
     assert _is_pow2(d_rope)
-    assert q.dtype == kv_cache.dtype
+    if kv_format == _lib.KV_SAME:
+        assert q.dtype == kv_cache.dtype
     if block_table is None:
         assert kv_cache.shape[0] == batch
     _require_cuda(q, kv_cache, cache_seqlens, block_table)
@@ -370,7 +378,7 @@ def mla_decode(
         lse.data_ptr(), lse.stride(0),
         ws_o, ws_lse, _status_word(device).data_ptr(),
         batch, num_heads, d_qk, head_dim_v, num_splits,
-        _DTYPE_CODES[q.dtype], _KERNELS[kernel], 0, float(softmax_scale), q_len,
+        _DTYPE_CODES[q.dtype], _KERNELS[kernel], 0, float(softmax_scale), q_len, kv_format,
     )
     prev = torch.cuda.current_device()
     if prev != device.index:
@@ -414,6 +422,7 @@ def selected_kernel(q, kv_cache, block_table=None, head_dim_v=512, num_splits=1,
     p.out_stride_b, p.out_stride_h = num_heads * head_dim_v, head_dim_v
     p.batch, p.num_heads, p.d_qk, p.d_v, p.num_splits = batch, num_heads, d_qk, head_dim_v, num_splits
     p.dtype, p.kernel, p.q_len = _DTYPE_CODES[q.dtype], _KERNELS[kernel], int(q_len)
+    p.kv_format = _lib.KV_FP8_E4M3 if kv_cache.dtype == torch.uint8 else _lib.KV_SAME
     k = _lib.load().tmla_select_kernel(ctypes.byref(p))
     if k < 0:
         raise _lib.LibraryError(-k, "tmla_select_kernel")
