@@ -67,9 +67,10 @@ __device__ __forceinline__ const unsigned char* fp8_row(const TmlaDecodeParams& 
   return base + (int64_t)page * p.kv_stride_page + (int64_t)(t - slot * p.page_size) * p.kv_stride_tok;
 }
 
-// Eight e4m3 values (one 8-byte word) times `scale`, as T.
+// Eight e4m3 values (one 8-byte word) times `scale`, in fp32.
 template <typename T>
 __device__ __forceinline__ void fp8x8_to(T* dst, uint2 w, float scale) {
+  static_assert(std::is_same<T, float>::value, "FP8 rows are dequantised to fp32");
   const uint32_t words[2] = {w.x, w.y};
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -77,8 +78,8 @@ __device__ __forceinline__ void fp8x8_to(T* dst, uint2 w, float scale) {
     for (int j = 0; j < 2; ++j) {
       const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[i] >> (16 * j)), __NV_E4M3);
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-      dst[4 * i + 2 * j] = Elem<T>::from_f(f.x * scale);
-      dst[4 * i + 2 * j + 1] = Elem<T>::from_f(f.y * scale);
+      dst[4 * i + 2 * j] = f.x * scale;
+      dst[4 * i + 2 * j + 1] = f.y * scale;
     }
   }
 }
@@ -93,7 +94,9 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
   float* m_s = p_s + kGenHeads * kGenTok;            // running max (base 2)
   float* l_s = m_s + kGenHeads;                      // running sum
   float* a_s = l_s + kGenHeads;                      // per-tile rescale factor
-  T* k_s = reinterpret_cast<T*>(a_s + kGenHeads);    // [32][Dk]
+  // FP8 rows are dequantised to fp32 (a 16-bit tile would round the scaled values again).
+  using KT = typename std::conditional<kFp8Cache, float, T>::type;
+  KT* k_s = reinterpret_cast<KT*>(a_s + kGenHeads);  // [32][Dk]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int h0 = blockIdx.x * kGenHeads, split = blockIdx.y, b = blockIdx.z;
@@ -139,20 +142,20 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
       for (int c = tid; c < kGenTok * 72; c += kGenThreads) {
         const int r = c / 72, k = c - r * 72, tok = t0 + r;
         const unsigned char* row = tok < end ? fp8_row(p, b, tok) : nullptr;
-        T* dst = k_s + r * Dk;
+        KT* dst = k_s + r * Dk;
         if (k < 64) {
           if (row) {
             const float scale = reinterpret_cast<const float*>(row + 512)[k >> 4];
-            fp8x8_to<T>(dst + 8 * k, *reinterpret_cast<const uint2*>(row + 8 * k), scale);
+            fp8x8_to<KT>(dst + 8 * k, *reinterpret_cast<const uint2*>(row + 8 * k), scale);
           } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) dst[8 * k + i] = st_f<T>(0.f);
+            for (int i = 0; i < 8; ++i) dst[8 * k + i] = 0.f;
           }
         } else {
           const int e = 8 * (k - 64);
           const __nv_bfloat16* rope = row ? reinterpret_cast<const __nv_bfloat16*>(row + 528) : nullptr;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) dst[512 + e + i] = rope ? Elem<T>::from_f(__bfloat162float(rope[e + i])) : st_f<T>(0.f);
+          for (int i = 0; i < 8; ++i) dst[512 + e + i] = rope ? __bfloat162float(rope[e + i]) : 0.f;
         }
       }
     } else if (vec_ok) {
@@ -189,9 +192,9 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int r = (tid & 15) + half * 16;
-        const T* kr = k_s + r * Dk;
+        const KT* kr = k_s + r * Dk;
         float s = 0.f;
-        for (int d = 0; d < D; ++d) s = fmaf(qr[d], ld_f<T>(kr + d), s);
+        for (int d = 0; d < D; ++d) s = fmaf(qr[d], ld_f<KT>(kr + d), s);
         p_s[h * kGenTok + r] = (t0 + r < row_end) ? s : -INFINITY;
       }
     }
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
 #pragma unroll
       for (int j = 0; j < kGenMaxCols; ++j) {
         const int d = tid + j * kGenThreads;
-        v[j] = (d < DV) ? ld_f<T>(k_s + t * Dk + d) : 0.f;
+        v[j] = (d < DV) ? ld_f<KT>(k_s + t * Dk + d) : 0.f;
       }
 #pragma unroll
       for (int h = 0; h < kGenHeads; ++h) {
@@ -295,10 +298,11 @@ static int launch_generic_t(const TmlaDecodeParams& p, cudaStream_t stream) {
     if (p.kv_format == TMLA_KV_FP8_E4M3) {
       // 8- and 16-byte loads from the rows: the base and the strides are 16-byte aligned.
       if (((uintptr_t)p.kv) % 16 || p.kv_stride_tok % 16 || p.kv_stride_page % 16) return TMLA_ERR_MISALIGNED;
+      const size_t smem8 = generic_smem_bytes(p.d_qk, (int)sizeof(float));
       e = cudaFuncSetAttribute(mla_generic_split_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem);
+                               (int)smem8);
       if (e != cudaSuccess) return -(int)e;
-      mla_generic_split_kernel<T, true><<<grid, kGenThreads, smem, stream>>>(p, 0);
+      mla_generic_split_kernel<T, true><<<grid, kGenThreads, smem8, stream>>>(p, 0);
       e = cudaGetLastError();
       return e == cudaSuccess ? 0 : -(int)e;
     }
