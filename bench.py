@@ -44,6 +44,7 @@ METRIC = "MLA decode µs/call and TFLOPS (H=128, bf16, paged) vs roofline at 1/2
 D_QK, D_V, PAGE = 576, 512, 64
 SCALE = 192 ** -0.5
 L2_FLUSH_BYTES = 256 << 20
+HOST_LEAD_CYCLES = 200_000  # ~0.1 ms of device-side wait before each timed step (outside the events)
 
 CONFIGS = {
     "cfg2": dict(desc="BASELINE config 2: B=32 H=128 S=4096 (all requests) page 64 bf16 paged, shuffled pages",
@@ -76,6 +77,31 @@ def decode_bytes(total_tokens, batch, heads, elt=2, row_bytes=None):
 NCU_TRAFFIC = {
     ("cfg2", "sm100"): (160.9e6, "profiles/mla_sm100_split_kernel__cfg2_B32_S4096.md"),
 }
+
+
+def bind_to_gpu_cpus(device_index):
+    """Run this process on the CPUs the driver reports as local to the GPU (NVML), so that its
+    pinned host buffers sit next to the GPU's PCIe link.  Returns the previous CPU set, or None
+    when NVML cannot tell.  Only reads the GPU's topology; changes nothing on the GPU."""
+    try:
+        import pynvml
+        import torch
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        before = os.sched_getaffinity(0)
+        cpus = {64 * w + bit for w, mask in enumerate(words) for bit in range(64) if (mask >> bit) & 1} & before
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return before
+    except Exception:  # noqa: BLE001 - best effort: no NVML, no topology, no permission
+        return None
 
 
 def peaks():
@@ -250,6 +276,8 @@ def run_layer(args, cfg, device, world, rank, local):
     peak = hbm if bound == "hbm" else tflops_peak
     cpu = None
     if world == 1 and args.cpu_budget > 0:
+        if getattr(args, "all_cpus", None):
+            os.sched_setaffinity(0, args.all_cpus)  # the CPU baseline runs on all of the host's cores
         cpu = cpu_layer_rate(layer, kv, bt, ctx, min(args.cpu_budget, 20.0))
     line = {
         "metric": METRIC, "value": world * flops / (ms_max * 1e-3) / 1e12, "unit": "TFLOPS", "n_gpus": world,
@@ -511,6 +539,7 @@ def main(argv=None):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    all_cpus = args.all_cpus = bind_to_gpu_cpus(local)
     device = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
@@ -576,6 +605,9 @@ def main(argv=None):
             dist.barrier()
         torch.cuda.synchronize()
         for i in range(args.steps):
+            # A short device-side wait first keeps the GPU ahead of the host: the events then
+            # bracket device work only, also when several ranks share the host's cores.
+            torch.cuda._sleep(HOST_LEAD_CYCLES)
             flush.zero_()
             starts[i].record(stream)
             step()
@@ -612,6 +644,7 @@ def main(argv=None):
         _lib.KV_FP8_E4M3 if args.kv_fp8 else _lib.KV_SAME)
     ks, ke = [], []
     for i in range(args.warmup + args.steps):
+        torch.cuda._sleep(HOST_LEAD_CYCLES)
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -730,6 +763,8 @@ def main(argv=None):
     }
     cpu = None
     if world == 1 and args.cpu_budget > 0:
+        if all_cpus:
+            os.sched_setaffinity(0, all_cpus)  # the CPU baseline runs on all of the host's cores
         rate, done, el = cpu_oracle_rate(args.cpu_budget)
         cpu = {"value": rate, "unit": "TFLOPS", "cores": os.cpu_count() or 1, "kind": "port",
                "sample": f"{done} requests x 4096 tokens x 128 heads of the workload in {el:.1f}s "
