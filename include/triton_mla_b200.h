@@ -266,7 +266,9 @@ int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream);
 
 /* out[b, h * d_v + d] = sum_c o[b, h, c] W_UV[h][d][c]: the decode output projected back per
    head, the input of wo (model.py:123).  Needs rank a multiple of 16 (<= 2048) and w_kv_b
-   16-byte aligned (else TMLA_ERR_MISALIGNED). */
+   16-byte aligned (else TMLA_ERR_MISALIGNED).  Up to 64 requests of a 16-bit dtype with
+   16-byte aligned o rows run on the projection kernel of tmla_linear (one group per head,
+   tile-aligned, no workspace); others on a mma.sync / CUDA-core kernel. */
 typedef struct TmlaOUnabsorbParams {
   const void* o;                   /* [batch, heads, rank]: mla_decode's output */
   int64_t o_stride_b, o_stride_h;
@@ -278,6 +280,46 @@ typedef struct TmlaOUnabsorbParams {
   int32_t flags;                   /* TMLA_LAYER_FLAG_* */
 } TmlaOUnabsorbParams;
 int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream);
+
+/* y[i, j] = sum_c x[i, c] w[j, c] for m <= 64 rows of x: a bias-free nn.Linear of a decode
+   batch (replaces the cuBLAS GEMMs behind the reference layer's wq_a, wkv_a, wq_b and wo,
+   model.py:104-108,124), streaming w once through tcgen05 MMAs on every SM.  With groups > 1
+   the same product is taken for each group g over x + g * x_group_stride,
+   w + g * w_group_stride and y + g * y_group_stride (per-head weights: the absorption
+   einsums of model.py:111-113,123).  w is stored [n][k] (TMLA_W_NK, nn.Linear) or [k][n]
+   (TMLA_W_KN) with rows w_stride apart.  Needs 16-bit x / w / y of one dtype; x and w
+   16-byte aligned with row and group strides a multiple of 8 elements (else
+   TMLA_ERR_MISALIGNED).  groups * ceil(n / 128) <= TMLA_LINEAR_MAX_TILES.  The workspace
+   (tmla_linear_workspace_bytes, 16-byte aligned) starts with TMLA_LINEAR_MAX_TILES int32 tile
+   counters, which must be zero before its first use; every call leaves them at zero again
+   (the partial sums after them need no initial value).  Calls that may run at the same
+   time (different streams) need separate workspaces.  With TMLA_LAYER_FLAG_PDL the weight loads may overlap the
+   preceding kernel, which must not write w. */
+#define TMLA_W_NK 0
+#define TMLA_W_KN 1
+#define TMLA_LINEAR_MAX_TILES 65536
+typedef struct TmlaLinearParams {
+  const void* x;                   /* [m, k] per group */
+  int64_t x_stride;
+  const void* w;                   /* [n, k] or [k, n] per group */
+  int64_t w_stride;
+  void* y;                         /* [m, n] per group */
+  int64_t y_stride;
+  int32_t m, n, k;
+  int32_t dtype;                   /* TMLA_DTYPE_BF16 or TMLA_DTYPE_FP16 */
+  void* workspace;
+  int64_t workspace_bytes;
+  int32_t num_sms;                 /* CTAs to spread the weight over (<= 0: the device's SM count) */
+  int32_t flags;                   /* TMLA_LAYER_FLAG_* */
+  int32_t* status;                 /* optional device status word (TMLA_STATUS_TIMEOUT) */
+  int32_t groups;                  /* >= 1 */
+  int32_t w_layout;                /* TMLA_W_NK or TMLA_W_KN */
+  int64_t x_group_stride, w_group_stride, y_group_stride;  /* elements; used when groups > 1 */
+} TmlaLinearParams;
+int tmla_linear(const TmlaLinearParams* p, void* stream);
+/* Workspace bytes tmla_linear needs for this shape and SM count, or -TMLA_ERR_INVALID_ARG.
+   Host-only. */
+int64_t tmla_linear_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t groups, int32_t num_sms);
 
 #ifdef __cplusplus
 }

@@ -219,3 +219,31 @@ def test_plan_units_device_rejects_bad_arguments():
     ]
     for args in bad:
         assert lib.tmla_plan_units_device(*args, None) == _lib.ERR_INVALID_ARG, args
+
+
+def _linear_plan(m, n, k, sms, groups=1):
+    """The projection kernel's work split, restated: units (group, 128-row tile, 128-column
+    k-step), in that order, cut into min(sms, units) equal contiguous ranges."""
+    tiles, steps = -(-n // 128) * groups, -(-k // 128)
+    units = tiles * steps
+    grid = min(sms, units)
+    owner = lambda u: ((u + 1) * grid - 1) // units  # noqa: E731
+    parts = max(owner(t * steps + steps - 1) - owner(t * steps) + 1 for t in range(tiles))
+    tok = 16 if m <= 16 else (32 if m <= 32 else 64)
+    counters = 65536 * 4  # TMLA_LINEAR_MAX_TILES counters, whatever the shape
+    return counters + (tiles * parts * tok * 128 * 4 if parts > 1 else 0)
+
+
+@pytest.mark.parametrize("m,n,k,sms,groups", [(16, 2112, 7168, 148, 1), (16, 24576, 1536, 148, 1),
+                                              (16, 7168, 16384, 148, 1), (1, 100, 64, 148, 1), (33, 257, 72, 148, 1),
+                                              (64, 1000, 512, 7, 1), (16, 128, 512, 148, 128), (16, 512, 128, 148, 128),
+                                              (3, 200, 72, 5, 9)])
+def test_linear_workspace_bytes(m, n, k, sms, groups):
+    assert _lib.load().tmla_linear_workspace_bytes(m, n, k, groups, sms) == _linear_plan(m, n, k, sms, groups)
+
+
+def test_linear_workspace_bytes_rejects_bad_shapes():
+    lib = _lib.load()
+    for args in [(0, 8, 8, 1, 148), (65, 8, 8, 1, 148), (4, 0, 8, 1, 148), (4, 8, 0, 1, 148), (4, 8, 8, 1, 0),
+                 (4, 8, 8, 0, 148)]:
+        assert lib.tmla_linear_workspace_bytes(*args) == -_lib.ERR_INVALID_ARG

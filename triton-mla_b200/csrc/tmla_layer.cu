@@ -96,7 +96,8 @@ __device__ __forceinline__ void rope_pair(float a, float b, int pos, int i, int 
                                           float& out_b) {
   const float inv_freq = powf(theta, -(float)(2 * i) / (float)d_rope);
   const float angle = (float)pos * inv_freq;
-  const float c = cosf(angle), s = sinf(angle);
+  float s, c;
+  sincosf(angle, &s, &c);
   out_a = a * c - b * s;
   out_b = b * c + a * s;
 }
@@ -589,6 +590,7 @@ cudaError_t launch(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  tmla::max_smem_carveout(kernel);
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
@@ -688,6 +690,29 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
   cudaError_t e = cudaSuccess;
+  if (p->dtype != TMLA_DTYPE_FP32 && p->batch <= 64 && (uintptr_t)p->o % 16 == 0 && p->o_stride_b % 8 == 0 &&
+      p->o_stride_h % 8 == 0 && ((size_t)p->d_nope * p->rank) % 8 == 0) {
+    // Up to 64 requests: the weight-streaming tcgen05 kernel, one group per head (W_UV[h] is
+    // [d_v][rank], the rows d_nope .. d_nope + d_v of the head's block of w_kv_b).
+    TmlaLinearParams lp = {};
+    lp.x = p->o;
+    lp.x_stride = p->o_stride_b;
+    lp.x_group_stride = p->o_stride_h;
+    lp.w = static_cast<const char*>(p->w_kv_b) + (size_t)p->d_nope * p->rank * 2;
+    lp.w_stride = p->rank;
+    lp.w_group_stride = (int64_t)(p->d_nope + p->d_v) * p->rank;
+    lp.w_layout = TMLA_W_NK;
+    lp.y = p->out;
+    lp.y_stride = p->out_stride_b;
+    lp.y_group_stride = p->d_v;
+    lp.m = p->batch;
+    lp.n = p->d_v;
+    lp.k = p->rank;
+    lp.groups = p->num_heads;
+    lp.dtype = p->dtype;
+    lp.flags = p->flags;
+    return tmla::linear_launch(lp, true, s);
+  }
   if (p->dtype != TMLA_DTYPE_FP32 && p->rank % 64 == 0 && p->d_v % 32 == 0) {
     // 16-bit types: the contraction on tensor cores (mma.sync m16n8k16, fp32 accumulation).
     const dim3 grid_mma(p->num_heads, p->d_v / 32);

@@ -24,6 +24,8 @@ ERR_MISALIGNED = 3
 ERR_CUDA = 4
 ERR_WORKSPACE = 5
 LAYER_FLAG_PDL = 1
+W_NK = 0
+W_KN = 1
 KV_SAME = 0
 KV_FP8_E4M3 = 1
 
@@ -62,6 +64,8 @@ EXPORTED = (
     "tmla_units_workspace_bytes",
     "tmla_decode_units",
     "tmla_plan_units_device",
+    "tmla_linear",
+    "tmla_linear_workspace_bytes",
 )
 
 
@@ -182,6 +186,33 @@ class TmlaOUnabsorbParams(ctypes.Structure):
     ]
 
 
+class TmlaLinearParams(ctypes.Structure):
+    """Mirror of ``TmlaLinearParams``."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("x_stride", ctypes.c_int64),
+        ("w", ctypes.c_void_p),
+        ("w_stride", ctypes.c_int64),
+        ("y", ctypes.c_void_p),
+        ("y_stride", ctypes.c_int64),
+        ("m", ctypes.c_int32),
+        ("n", ctypes.c_int32),
+        ("k", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
+        ("num_sms", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+        ("groups", ctypes.c_int32),
+        ("w_layout", ctypes.c_int32),
+        ("x_group_stride", ctypes.c_int64),
+        ("w_group_stride", ctypes.c_int64),
+        ("y_group_stride", ctypes.c_int64),
+    ]
+
+
 class LibraryError(RuntimeError):
     """A non-zero return code from the C ABI."""
 
@@ -239,8 +270,10 @@ def load() -> ctypes.CDLL:
     lib.tmla_decode_units.restype = ctypes.c_int
     lib.tmla_plan_units_device.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp, vp]
     lib.tmla_plan_units_device.restype = ctypes.c_int
+    lib.tmla_linear_workspace_bytes.argtypes = [i32, i32, i32, i32, i32]
+    lib.tmla_linear_workspace_bytes.restype = i64
     for name, st in (("tmla_q_absorb_rope", TmlaQPrepParams), ("tmla_kv_norm_rope_append", TmlaKvAppendParams),
-                     ("tmla_o_unabsorb", TmlaOUnabsorbParams)):
+                     ("tmla_o_unabsorb", TmlaOUnabsorbParams), ("tmla_linear", TmlaLinearParams)):
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(st), vp]
         fn.restype = ctypes.c_int

@@ -1,9 +1,11 @@
 """The MLA layer's per-step operations around the decode kernel, one CUDA launch each
-(C ABI: ``tmla_q_absorb_rope``, ``tmla_kv_norm_rope_append``, ``tmla_o_unabsorb``).
+(C ABI: ``tmla_q_absorb_rope``, ``tmla_kv_norm_rope_append``, ``tmla_o_unabsorb``,
+``tmla_linear``).
 
 They replace the PyTorch glue of the reference's ``MLA.forward``
 (src/triton_mla/model.py:74-94 and 111-123): RoPE of q_pe and k_pe, kv_norm, the
-paged-cache append, the absorption einsums by W_UK / W_UV and the concatenation.
+paged-cache append, the absorption einsums by W_UK / W_UV and the concatenation;
+and, for decode batches of up to 64 tokens, the projections' GEMMs (model.py:104-108, 124).
 """
 
 from __future__ import annotations
@@ -100,3 +102,93 @@ def o_unabsorb(o: torch.Tensor, w_kv_b: torch.Tensor, d_nope: int, d_v: int, ove
                                  _lib.LAYER_FLAG_PDL if overlap else 0)
     _lib.check(_lib.load().tmla_o_unabsorb(ctypes.byref(p), _stream(o)), "tmla_o_unabsorb")
     return out
+
+
+# ----------------------------------------------------------------------------- projections
+LINEAR_MAX_TOKENS = 64
+
+
+def linear_ok(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether ``linear`` takes ``x @ weight.T``: CUDA tensors of one 16-bit dtype, at most 64
+    rows of x, 16-byte aligned rows (k a multiple of 8) and a row-major weight."""
+    if not (x.is_cuda and x.dim() == 2 and weight.dim() == 2 and x.dtype in (torch.bfloat16, torch.float16)):
+        return False
+    if weight.dtype != x.dtype or weight.device != x.device or x.shape[1] != weight.shape[1]:
+        return False
+    m, k = x.shape
+    return (0 < m <= LINEAR_MAX_TOKENS and k % 8 == 0 and x.stride(-1) == 1 and x.stride(0) % 8 == 0
+            and weight.stride(-1) == 1 and weight.stride(0) % 8 == 0
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0)
+
+
+# Below this many weight bytes cuBLAS wins inside the layer step: the projection kernel's
+# fixed costs (a cold start, the ordered sum of split-K partials) outweigh its streaming rate
+# (measured on B200 in the DeepSeek-V3 layer graph: [wq_a; wkv_a], 30 MB, 16.9 us against
+# cuBLAS's 13.0 us; wq_b, 75 MB, finished 2.7 us sooner than cuBLAS).
+LINEAR_MIN_WEIGHT_BYTES = 48 << 20
+
+
+def linear_preferred(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether a layer step should take ``linear`` for ``x @ weight.T`` rather than cuBLAS."""
+    return linear_ok(x, weight) and weight.numel() * weight.element_size() >= LINEAR_MIN_WEIGHT_BYTES
+
+
+def linear_workspace_bytes(m: int, n: int, k: int, num_sms: int, groups: int = 1) -> int:
+    """Workspace bytes of ``linear`` for x [m, k], weight [n, k] (per group) spread over
+    ``num_sms`` SMs."""
+    need = _lib.load().tmla_linear_workspace_bytes(m, n, k, groups, num_sms)
+    if need < 0:
+        _lib.check(-need, "tmla_linear_workspace_bytes")
+    return need
+
+
+class LinearWorkspace:
+    """Counters and partial sums of ``linear`` for calls on one stream at a time.  Grows on
+    demand; a grown-out buffer is kept alive, because a captured CUDA graph may still use it.
+    The kernel leaves the counters at zero, so the buffer is zero-filled only when made."""
+
+    def __init__(self):
+        self.buf = None
+        self._retired = []
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        if self.buf is None or self.buf.device != device or self.buf.numel() < nbytes:
+            if self.buf is not None:
+                self._retired.append(self.buf)
+            self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        return self.buf
+
+
+_stream_ws = {}
+
+
+def _linear_launch(x, x_stride, x_gstride, w, w_stride, w_gstride, w_layout, y, y_stride, y_gstride,
+                   m, n, k, groups, overlap, workspace):
+    sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+    need = linear_workspace_bytes(m, n, k, sms, groups)
+    if workspace is None:
+        key = (x.device.index, torch.cuda.current_stream(x.device).cuda_stream)
+        workspace = _stream_ws.setdefault(key, LinearWorkspace())
+    ws = workspace.get(x.device, need)
+    p = _lib.TmlaLinearParams(x.data_ptr(), x_stride, w.data_ptr(), w_stride, y.data_ptr(), y_stride,
+                              m, n, k, _DTYPE_CODES[x.dtype], ws.data_ptr(), ws.numel(), sms,
+                              _lib.LAYER_FLAG_PDL if overlap else 0, _status_word(x.device).data_ptr(),
+                              groups, w_layout, x_gstride, w_gstride, y_gstride)
+    _lib.check(_lib.load().tmla_linear(ctypes.byref(p), _stream(x)), "tmla_linear")
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, overlap: bool = False,
+           workspace: LinearWorkspace | None = None) -> torch.Tensor:
+    """``x @ weight.T`` (``F.linear`` without bias) for a decode batch of at most 64 rows, with
+    the weight streamed once through tcgen05 MMAs on every SM (C ABI: ``tmla_linear``).
+    ``overlap``: launch as a programmatic dependent of the preceding kernel in the stream,
+    whose end then overlaps the first weight loads; that kernel must not write ``weight``.
+    ``workspace``: a ``LinearWorkspace`` not used by another stream at the same time
+    (default: one per device and stream)."""
+    assert linear_ok(x, weight), "linear: 16-bit CUDA x [m <= 64, k] and weight [n, k], 16-byte aligned rows"
+    m, k = x.shape
+    n = weight.shape[0]
+    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    _linear_launch(x, x.stride(0), 0, weight, weight.stride(0), 0, _lib.W_NK, y, n, 0, m, n, k, 1, overlap,
+                   workspace)
+    return y

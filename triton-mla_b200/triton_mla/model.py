@@ -9,12 +9,15 @@ num_splits=None) -> (out, seqlens)`` appends the new token in place and runs
 the absorbed decode (model.py:101-124); ``MLA.forward_naive`` is the
 decompressed form (model.py:126-144).
 
-The attention step is ``mla_decode`` (CUDA library).  The projections are
-cuBLAS GEMMs (``nn.Linear``) and q_norm is PyTorch's RMSNorm; the rest of a
-decode step runs as three fused CUDA launches (``layer_ops``): the kv_norm,
-k_pe RoPE and cache append; the q_pe RoPE, absorption by W_UK and concatenation
-into the decode query; and the W_UV projection of the decode output.  Steps
-whose tensors do not share one dtype take the PyTorch-op form of the same math.
+The attention step is ``mla_decode`` (CUDA library).  For up to 64 tokens of one
+16-bit dtype the large projections (``wq_b``, ``wo``) are the library's
+weight-streaming tcgen05 GEMM (``layer_ops.linear``), the others cuBLAS (``wq_a``
+and ``wkv_a`` as one GEMM).  The rest
+of a decode step runs as three fused CUDA launches (``layer_ops``): the kv_norm,
+k_pe RoPE and cache append, with q_norm in the same launch; the q_pe RoPE,
+absorption by W_UK and concatenation into the decode query; and the W_UV
+projection of the decode output.  Steps whose tensors do not share one dtype take
+the PyTorch-op form of the same math.
 """
 
 from __future__ import annotations
@@ -133,10 +136,26 @@ class MLA(nn.Module):
             self._w_a_key = key
         return self._w_a_cat
 
+    def _linear_ws(self):
+        """The projection kernel's workspace of this layer (its steps run on one stream at a time)."""
+        ws = self.__dict__.get("_linear_workspace")
+        if ws is None:
+            ws = self.__dict__["_linear_workspace"] = layer_ops.LinearWorkspace()
+        return ws
+
+    def _proj(self, inp, weight, overlap):
+        """``F.linear(inp, weight)``: the weight-streaming tcgen05 kernel for up to 64 tokens and
+        a large weight (``layer_ops.linear_preferred``), else cuBLAS.  ``overlap`` as in
+        ``layer_ops.linear``."""
+        if layer_ops.linear_preferred(inp, weight):
+            return layer_ops.linear(inp, weight, overlap=overlap, workspace=self._linear_ws())
+        return F.linear(inp, weight)
+
     def _forward_fused(self, x, kv_cache, cache_seqlens, block_table, num_splits):
         cfg = self.cfg
         batch = x.shape[0]
-        qa, kva = F.linear(x, self._w_a()).split([cfg.q_lora_rank, cfg.kv_cache_dim], dim=-1)
+        # The first GEMM is an ordinary launch: the kernel before it may have written a weight.
+        qa, kva = self._proj(x, self._w_a(), False).split([cfg.q_lora_rank, cfg.kv_cache_dim], dim=-1)
         positions = cache_seqlens.to(torch.int32).contiguous()
         bt = None if block_table is None else block_table.to(torch.int32).contiguous()
         seqlens = torch.empty_like(positions)
@@ -146,13 +165,13 @@ class MLA(nn.Module):
         qn = layer_ops.kv_norm_rope_append(kva, self.kv_norm.weight, positions, kv_cache, bt, self.kv_norm.eps,
                                            cfg.rope_theta, seqlens_out=seqlens, overlap=True, q_in=qa,
                                            q_norm_weight=self.q_norm.weight, q_eps=self.q_norm.eps)
-        q = self.wq_b(qn).view(batch, cfg.num_heads, cfg.qk_head_dim)
+        q = self._proj(qn, self.wq_b.weight, True).view(batch, cfg.num_heads, cfg.qk_head_dim)
         q_full = layer_ops.q_absorb_rope(q, self.wkv_b.weight, positions, cfg.qk_nope_head_dim, cfg.v_head_dim,
                                          cfg.rope_theta, overlap=True)
         o = mla_decode(q_full, kv_cache, seqlens, bt, head_dim_v=cfg.kv_lora_rank, softmax_scale=self.softmax_scale,
                        num_splits=num_splits)
         o = layer_ops.o_unabsorb(o, self.wkv_b.weight, cfg.qk_nope_head_dim, cfg.v_head_dim, overlap=True)
-        return self.wo(o), seqlens.to(cache_seqlens.dtype)
+        return self._proj(o, self.wo.weight, True), seqlens.to(cache_seqlens.dtype)
 
     def _forward_ops(self, x, kv_cache, cache_seqlens, block_table, num_splits):
         """The decode step as PyTorch ops around ``mla_decode`` (mixed dtypes)."""
