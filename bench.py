@@ -195,6 +195,13 @@ def run_layer(args, cfg, device, world, rank, local):
     lens = torch.full((B,), ctx, dtype=torch.int32, device=device)
     x = torch.randn(B, mcfg.hidden_size, generator=g, device=device, dtype=torch.bfloat16)
     splits = get_num_splits(B, 128, ctx + 1, torch.cuda.get_device_properties(device).multi_processor_count)
+    # The library's launches per step: kv append (+ q_norm), q absorb, W_UV, the decode (+ merge),
+    # and the wq_b / wo projections that take the tcgen05 projection kernel.
+    from triton_mla import layer_ops
+    q_rows = torch.empty(B, mcfg.q_lora_rank, device=device, dtype=torch.bfloat16)
+    o_rows = torch.empty(B, mcfg.num_heads * mcfg.v_head_dim, device=device, dtype=torch.bfloat16)
+    layer_launches = 3 + (2 if splits > 1 else 1) + sum(
+        layer_ops.linear_preferred(a, w) for a, w in ((q_rows, layer.wq_b.weight), (o_rows, layer.wo.weight)))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     flops, nbytes = layer_counts(B, ctx)
@@ -291,14 +298,15 @@ def run_layer(args, cfg, device, world, rank, local):
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
                      "frac": achieved / peak, "traffic": None, "traffic_source": "not captured for this config",
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
-                     "kernel": "whole layer step (cuBLAS projections + tcgen05 decode)",
+                     "kernel": "whole layer step (tcgen05 decode and wq_b / wo / W_UV projections, "
+                               "cuBLAS wq_a + wkv_a)",
                      "algorithmic_bytes_per_step": nbytes, "algorithmic_flops_per_step": flops},
         "cpu_baseline": cpu,
         "e2e": {"value": world * flops / (float(te.item()) * 1e-3) / 1e12, "unit": "TFLOPS",
                 "ms_per_step": float(te.item()), "h2d_bytes_per_step": x_h.numel() * 2,
                 "d2h_bytes_per_step": out_h.numel() * 2,
                 "note": "per step: x host->device, layer output device->host; weights and cache resident"},
-        "gpu_launches": args.steps * (1 + (1 if splits > 1 else 0)),
+        "gpu_launches": args.steps * layer_launches,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
