@@ -296,16 +296,13 @@ static int launch_combine_t(const float* ws_o, const float* ws_lse, void* out, i
   if (vec_ok && DV == 512 && S <= 4) {
     cfg.blockDim = dim3(kRowWarps * 32);
     cfg.gridDim = dim3((unsigned)((rows + kRowWarps - 1) / kRowWarps));
-    max_smem_carveout(mla_combine_row512_kernel<T>);
     e = cudaLaunchKernelEx(&cfg, mla_combine_row512_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S);
   } else if (vec_ok) {
     const int64_t warps = rows * (DV / 128);
     cfg.gridDim = dim3((unsigned)((warps + kCombineWarps - 1) / kCombineWarps));
-    max_smem_carveout(mla_combine_vec_kernel<T>);
     e = cudaLaunchKernelEx(&cfg, mla_combine_vec_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
   } else {
     cfg.gridDim = dim3((unsigned)((rows + kCombineWarps - 1) / kCombineWarps));
-    max_smem_carveout(mla_combine_kernel<T>);
     e = cudaLaunchKernelEx(&cfg, mla_combine_kernel<T>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -327,7 +324,6 @@ static int launch_combine_slots_t(const float* ws_o, const float* ws_lse, const 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  max_smem_carveout(mla_combine_slots_kernel<T>);
   cudaError_t e = cudaLaunchKernelEx(&cfg, mla_combine_slots_kernel<T>, ws_o, ws_lse, req_first, static_cast<T*>(out),
                                      osb, osh, lse, lsb, B, H, DV);
   if (e == cudaSuccess) e = cudaGetLastError();

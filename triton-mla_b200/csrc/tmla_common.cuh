@@ -62,16 +62,6 @@ __device__ __forceinline__ void split_range(int len, int num_splits, int s, int&
   end = min(start + per * 64, len);
 }
 
-// Every kernel of the library runs with the largest shared-memory carveout.  A layer step is
-// a chain of kernels launched as programmatic dependents; with one carveout for all of them an
-// SM never drains to change its L1 / shared-memory split between two of them, and the CTAs of
-// a dependent can be placed beside those of the kernel before it.
-template <typename Kernel>
-inline cudaError_t max_smem_carveout(Kernel* kernel) {
-  return cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel), cudaFuncAttributePreferredSharedMemoryCarveout,
-                              (int)cudaSharedmemCarveoutMaxShared);
-}
-
 // The projection kernel behind tmla_linear, for the library's own callers too: with
 // tile_aligned every CTA takes whole 128-row tiles (no partial sums, no workspace).
 int linear_launch(const TmlaLinearParams& p, bool tile_aligned, cudaStream_t stream);

@@ -302,13 +302,11 @@ static int launch_generic_t(const TmlaDecodeParams& p, cudaStream_t stream) {
       e = cudaFuncSetAttribute(mla_generic_split_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem8);
       if (e != cudaSuccess) return -(int)e;
-      max_smem_carveout(mla_generic_split_kernel<T, true>);
       mla_generic_split_kernel<T, true><<<grid, kGenThreads, smem8, stream>>>(p, 0);
       e = cudaGetLastError();
       return e == cudaSuccess ? 0 : -(int)e;
     }
   }
-  max_smem_carveout(mla_generic_split_kernel<T, false>);
   mla_generic_split_kernel<T, false><<<grid, kGenThreads, smem, stream>>>(p, vec_ok);
   e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;

@@ -590,7 +590,6 @@ cudaError_t launch(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  tmla::max_smem_carveout(kernel);
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 

@@ -533,7 +533,6 @@ cudaError_t launch(const CUtensorMap& tw, const CUtensorMap& tx, const Args& a, 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  max_smem_carveout(linear_m16_kernel<T, kTok>);
   return cudaLaunchKernelEx(&cfg, linear_m16_kernel<T, kTok>, tw, tx, a);
 }
 

@@ -333,7 +333,6 @@ int tmla_plan_units_device(const int32_t* seqlens, int32_t batch, int32_t num_he
   const int head_tiles = (num_heads + 127) / 128;
   const int machines = std::max(1, num_sms / 2 / head_tiles);
   const size_t smem = sizeof(int) * (size_t)std::min<int>(batch, tmla::kTilesInSmem);
-  tmla::max_smem_carveout(tmla::plan_units_kernel);
   tmla::plan_units_kernel<<<tmla::kPlanCtas, tmla::kPlanThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       seqlens, batch, machines, capacity, slot_capacity, reinterpret_cast<int4*>(units), req_first);
   const cudaError_t e = cudaGetLastError();

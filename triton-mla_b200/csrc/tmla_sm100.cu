@@ -1156,13 +1156,11 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   if (p.dtype == TMLA_DTYPE_FP16) {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      max_smem_carveout(mla_sm100_split_kernel<__half>);
       e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__half>, tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
   } else {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
     if (e == cudaSuccess)
-      max_smem_carveout(mla_sm100_split_kernel<__nv_bfloat16>);
       e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__nv_bfloat16>, tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
