@@ -215,10 +215,11 @@ __global__ void __launch_bounds__(128) q_absorb_rope_kernel(TmlaQPrepParams p) {
       }
     }
   }
-  if (blockIdx.y == 0) {
-    // RoPE of q_pe for every request of this head.
+  {
+    // RoPE of q_pe for every request of this head, spread over the head's CTAs (one pair or
+    // two per thread, so that no CTA carries a chain of them).
     const int half = dr / 2;
-    for (int i = tid; i < p.batch * half; i += blockDim.x) {
+    for (int i = blockIdx.y * blockDim.x + tid; i < p.batch * half; i += gridDim.y * blockDim.x) {
       const int b = i / half, k = i % half;
       const T* src = q_in + (int64_t)b * p.q_in_stride_b + (int64_t)h * p.q_in_stride_h + dn;
       float oa, ob;
@@ -507,9 +508,10 @@ __global__ void __launch_bounds__(128) q_absorb_rope_mma_kernel(TmlaQPrepParams 
         st_pair(q_out + (int64_t)bb * p.q_out_stride_b + (int64_t)h * p.q_out_stride_h + c, acc[nt][2], acc[nt][3]);
     }
   }
-  if (blockIdx.y == 0) {
+  {
+    // RoPE of q_pe, spread over the head's CTAs like the kernel above.
     const int half = dr / 2;
-    for (int i = threadIdx.x; i < p.batch * half; i += blockDim.x) {
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < p.batch * half; i += gridDim.y * blockDim.x) {
       const int b = i / half, k = i % half;
       const T* src = q_in + (int64_t)b * p.q_in_stride_b + (int64_t)h * p.q_in_stride_h + dn;
       float oa, ob;
