@@ -2,33 +2,34 @@
 //
 //   y[m, n] = sum_k x[m, k] w[n, k]      (nn.Linear without bias: y = x w^T)
 //
-// for a few tokens (m <= 64) against a large weight, optionally for several groups
-// (per-head weights, such as W_UV in tmla_o_unabsorb) at once.  The layer's four projections (wq_a + wkv_a as one GEMM,
-// wq_b, wo: src/triton_mla/model.py:104-108 and 124 of the reference) read 374 MB of
-// weights per step for 16 tokens per GPU, so the work is a stream of the weight through
-// the tensor cores at HBM speed.  The weight of a group is stored [n][k] (nn.Linear) or
-// [k][n] (an einsum operand such as W_UK); the MMA reads either layout from shared memory.
+// for a few tokens (m <= 64) against a large weight, optionally for several groups at once
+// (per-head weights, such as W_UV in tmla_o_unabsorb).  The layer's projections (wq_a + wkv_a
+// as one GEMM, wq_b, wo: src/triton_mla/model.py:104-108 and 124 of the reference) read
+// 374 MB of weights per step for 16 tokens per GPU, so the work is a stream of the weight
+// through the tensor cores at HBM speed.  The weight of a group is stored [n][k] (nn.Linear)
+// or [k][n] (an einsum operand); the MMA reads either layout from shared memory.
 //
-// Layout of the work.  The weight is cut into tiles of 128 rows (outputs, the MMA's M)
-// by 64 columns (one 128-byte swizzle row of 16-bit values, a "k-step").  The units
-// (group, tile, k-step), in that order, are split into `grid` contiguous ranges of equal length,
-// one per CTA (one CTA per SM, persistent).  A CTA's range covers the end of one tile,
-// whole tiles and the start of another; each piece is a "segment".
+// Layout of the work.  The weight is cut into tiles of 128 rows (outputs, the MMA's M) by
+// kStepK = 128 columns (a "k-step": two 64-column TMA boxes with 128-byte swizzled rows, so
+// every weight row is read in 256 contiguous bytes).  The units (group, tile, k-step), in that
+// order, are split into `grid` contiguous ranges of equal length, one per CTA (one CTA per SM,
+// persistent).  A CTA's range covers the end of one tile, whole tiles and the start of
+// another; each piece is a "segment".  With tile_aligned the ranges hold whole tiles.
 //
 // Per CTA (192 threads):
-//   warp 0   TMA producer: per k-step, one 16 KB box of the weight (evict-first) and
-//            one box of x (tokens x 64 columns, evict-last: every tile re-reads it)
-//            into a ring of `stages` stages.  Weight boxes of the first stages are
-//            requested before griddepcontrol.wait: under a programmatic launch they
-//            overlap the preceding kernel, which must not write the weight.
-//   warp 1   MMA issuer: tcgen05.mma kind::f16, M = 128 (weight rows), N = tokens
-//            rounded up to 16, both operands K-major from shared memory, into one of
-//            two TMEM accumulators (double-buffered across segments).
+//   warp 0   TMA producer: per k-step, the weight boxes (evict-first) and the boxes of x
+//            (tokens x 64 columns, evict-last: every tile re-reads them) into a ring of
+//            `stages` stages.  The weight boxes of the first TMLA_LIN_EARLY stages are
+//            requested before griddepcontrol.wait: under a programmatic launch they overlap
+//            the preceding kernel, which must not write the weight.
+//   warp 1   MMA issuer: tcgen05.mma kind::f16, M = 128 (weight rows), N = tokens rounded
+//            up to 16, from shared memory (weight K-major or MN-major, x K-major), into one
+//            of two TMEM accumulators (double-buffered across segments).
 //   warps 2-5  epilogue: one thread per weight row (TMEM lane).  A tile covered by one
-//            segment is written to y directly.  Otherwise each segment writes its
-//            fp32 partial into its slot of the workspace and counts itself on the
-//            tile's counter; the last one sums the slots in slot order (so the result
-//            does not depend on timing), writes y and resets the counter to zero.
+//            segment is written to y directly.  Otherwise each segment writes its fp32
+//            partial into its slot of the workspace and counts itself on the tile's
+//            counter; the last one sums the slots in slot order (so the result does not
+//            depend on timing), writes y and resets the counter to zero.
 //
 // Every wait is bounded (2 s): on expiry the kernel sets TMLA_STATUS_TIMEOUT, stops,
 // drains the copies and MMAs it issued, frees TMEM and returns.  No CTA waits on
