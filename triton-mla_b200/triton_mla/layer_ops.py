@@ -123,8 +123,9 @@ def linear_ok(x: torch.Tensor, weight: torch.Tensor) -> bool:
 
 # Below this many weight bytes cuBLAS wins inside the layer step: the projection kernel's
 # fixed costs (a cold start, the ordered sum of split-K partials) outweigh its streaming rate
-# (measured on B200 in the DeepSeek-V3 layer graph: [wq_a; wkv_a], 30 MB, 16.9 us against
-# cuBLAS's 13.0 us; wq_b, 75 MB, finished 2.7 us sooner than cuBLAS).
+# (measured on B200, DeepSeek-V3 layer graph: with [wq_a; wkv_a] (30 MB, 9 split-K pieces per
+# tile) on this kernel the step took 169.1-169.4 us, with it on cuBLAS 168.4 us; wq_b (75 MB)
+# and wo (235 MB) on this kernel beat cuBLAS).
 LINEAR_MIN_WEIGHT_BYTES = 48 << 20
 
 
