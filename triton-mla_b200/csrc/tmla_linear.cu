@@ -78,7 +78,10 @@ constexpr int kEpiThreads = 128;
 constexpr int kAccCols = 64;                 // TMEM columns per accumulator buffer
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kMaxTokens = 64;
-constexpr uint32_t kSmemBudget = 192 * 1024;  // stage ring
+#ifndef TMLA_LIN_RING_KB
+#define TMLA_LIN_RING_KB 192
+#endif
+constexpr uint32_t kSmemBudget = TMLA_LIN_RING_KB * 1024;  // stage ring
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 // Barrier area after the ring: full[kMaxStages], empty[kMaxStages], acc_full[2],
