@@ -247,3 +247,43 @@ def test_linear_workspace_bytes_rejects_bad_shapes():
     for args in [(0, 8, 8, 1, 148), (65, 8, 8, 1, 148), (4, 0, 8, 1, 148), (4, 8, 0, 1, 148), (4, 8, 8, 1, 0),
                  (4, 8, 8, 0, 148)]:
         assert lib.tmla_linear_workspace_bytes(*args) == -_lib.ERR_INVALID_ARG
+
+
+def _linear_params(**kw):
+    """TmlaLinearParams with fake (aligned, never dereferenced) pointers: every case below is
+    rejected by the argument checks before any CUDA call."""
+    p = _lib.TmlaLinearParams()
+    p.x, p.w, p.y = 4096, 8192, 12288
+    p.m, p.n, p.k, p.groups = 16, 256, 512, 1
+    p.x_stride, p.w_stride, p.y_stride = 512, 512, 256
+    p.dtype, p.w_layout, p.num_sms = _lib.DTYPE_BF16, _lib.W_NK, 148
+    for key, value in kw.items():
+        setattr(p, key, value)
+    return p
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(x=None), _lib.ERR_INVALID_ARG),
+    (dict(dtype=_lib.DTYPE_FP32), _lib.ERR_UNSUPPORTED),
+    (dict(m=0), _lib.ERR_INVALID_ARG),
+    (dict(m=65), _lib.ERR_INVALID_ARG),
+    (dict(groups=0), _lib.ERR_INVALID_ARG),
+    (dict(w_layout=7), _lib.ERR_INVALID_ARG),
+    (dict(x_stride=256), _lib.ERR_INVALID_ARG),
+    (dict(w_layout=_lib.W_KN, w_stride=128), _lib.ERR_INVALID_ARG),
+    (dict(x=4104), _lib.ERR_MISALIGNED),
+    (dict(x_stride=516), _lib.ERR_MISALIGNED),
+    (dict(groups=2, w_group_stride=4), _lib.ERR_MISALIGNED),
+    (dict(), _lib.ERR_WORKSPACE),  # no workspace: 256 x 512 on 148 SMs cuts tiles
+])
+def test_linear_rejects_bad_arguments_before_any_launch(kw, code):
+    p = _linear_params(**kw)
+    assert _lib.load().tmla_linear(ctypes.byref(p), None) == code
+
+
+def test_linear_helpers_refuse_cpu_tensors():
+    from triton_mla import layer_ops
+    x, w = torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(64, 64, dtype=torch.bfloat16)
+    assert not layer_ops.linear_ok(x, w) and not layer_ops.linear_preferred(x, w)
+    with pytest.raises(AssertionError):
+        layer_ops.linear(x, w)
