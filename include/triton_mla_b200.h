@@ -292,8 +292,9 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream);
    TMLA_ERR_MISALIGNED).  groups * ceil(n / 128) <= TMLA_LINEAR_MAX_TILES.  The workspace
    (tmla_linear_workspace_bytes, 16-byte aligned) starts with TMLA_LINEAR_MAX_TILES int32 tile
    counters, which must be zero before its first use; every call leaves them at zero again
-   (the partial sums after them need no initial value).  Calls that may run at the same
-   time (different streams) need separate workspaces.  With TMLA_LAYER_FLAG_PDL the weight loads may overlap the
+   (the partial sums after them need no initial value).  After a call that set
+   TMLA_STATUS_TIMEOUT, zero the counters again: a piece that gave up was never counted.
+   Calls that may run at the same time (different streams) need separate workspaces.  With TMLA_LAYER_FLAG_PDL the weight loads may overlap the
    preceding kernel, which must not write w. */
 #define TMLA_W_NK 0
 #define TMLA_W_KN 1

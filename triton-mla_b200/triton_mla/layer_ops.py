@@ -152,6 +152,12 @@ class LinearWorkspace:
         self.buf = None
         self._retired = []
 
+    def clear(self) -> None:
+        """Zero the buffer: needed only after a call that set ``STATUS_TIMEOUT`` (read with
+        ``read_status``), whose pieces that gave up were never counted."""
+        if self.buf is not None:
+            self.buf.zero_()
+
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
         if self.buf is None or self.buf.device != device or self.buf.numel() < nbytes:
             if self.buf is not None:
