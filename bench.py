@@ -9,9 +9,12 @@ resident in HBM, L2 flushed (256 MiB write) before every timed step, each step
 timed with CUDA events on the launching stream.
 
 Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): requests are
-independent, so every rank decodes its own batch from its own page pool; there
-is no collective on the data path (NCCL only for barriers and the max-over-ranks
-timing).  Scaling is weak: per-GPU work is fixed.
+independent, so the config's batch is split over the ranks (equal contiguous
+slices, or token-balanced shards of the ragged config) and every rank decodes its
+share from its own page pool; there is no collective on the data path (NCCL only
+for barriers, the per-rank times and the max-over-ranks timing).  Scaling is
+strong: the total work is fixed.  ``--weak`` gives every rank a whole batch of a
+uniform config instead.
 
 ``--config cfg5`` times one decode step of the full MLA layer instead (BASELINE
 config 5: DeepSeek-V3 dims, random-init weights, 16 requests per GPU with 8192
@@ -72,13 +75,6 @@ def decode_bytes(total_tokens, batch, heads, elt=2, row_bytes=None):
     return float(rows + (batch * heads * D_QK + batch * heads * D_V) * elt)
 
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant kernel,
-# from the ncu capture summarised in profiles/ (re-captured whenever the kernel changes).
-NCU_TRAFFIC = {
-    ("cfg2", "sm100"): (160.9e6, "profiles/mla_sm100_split_kernel__cfg2_B32_S4096.md"),
-}
-
-
 def bind_to_gpu_cpus(device_index):
     """Run this process on the CPUs the driver reports as local to the GPU (NVML), so that its
     pinned host buffers sit next to the GPU's PCIe link.  Returns the previous CPU set, or None
@@ -134,15 +130,20 @@ def make_workload(cfg, device, seed):
 
 
 def make_sharded_workload(cfg, device, seed, rank, world):
-    """One global ragged batch (the same lengths on every rank, from ``seed``) split over the
-    ranks by token count (longest first onto the least-loaded rank); this rank builds only
+    """One global batch of the config (the same lengths on every rank, from ``seed``) split
+    over the ranks: equal contiguous slices of a uniform batch, or, for the ragged config,
+    token-balanced shards (longest first onto the least-loaded rank).  This rank builds only
     its own requests' q rows, page pool and block table.  Returns the rank's inputs and the
     global token count and batch size."""
     import torch
-    from triton_mla.sharding import balance_requests
+    from triton_mla.sharding import balance_requests, contiguous_requests
     gen_cpu = torch.Generator().manual_seed(seed)
-    lens_all = torch.randint(1, cfg["seqlen"] + 1, (cfg["batch"],), generator=gen_cpu, dtype=torch.int32)
-    reqs = balance_requests(lens_all.tolist(), world)[rank]
+    if cfg["ragged"]:
+        lens_all = torch.randint(1, cfg["seqlen"] + 1, (cfg["batch"],), generator=gen_cpu, dtype=torch.int32)
+        reqs = balance_requests(lens_all.tolist(), world)[rank]
+    else:
+        lens_all = torch.full((cfg["batch"],), cfg["seqlen"], dtype=torch.int32)
+        reqs = contiguous_requests(cfg["batch"], world)[rank]
     lens = lens_all[reqs]
     need = (lens + PAGE - 1) // PAGE
     num_pages = max(1, int(need.sum()))
@@ -531,6 +532,9 @@ def main(argv=None):
                     help="query tokens per request (multi-token decode, e.g. speculative / MTP); 1 = the reference's")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle timing (rank 0, N=1)")
     ap.add_argument("--clock-soak", type=float, default=0.6, help="seconds of untimed steps under the clock sampler")
+    ap.add_argument("--weak", action="store_true",
+                    help="weak scaling for a uniform config: every rank decodes a whole batch of it "
+                         "(default: the config's batch split over the ranks)")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -556,9 +560,10 @@ def main(argv=None):
     cfg = CONFIGS[args.config]
     if cfg.get("layer"):
         return run_layer(args, cfg, device, world, rank, local)
-    # Uniform configs scale weakly (every rank decodes its own batch of the config); the
-    # ragged config scales strongly (one global batch, token-balanced over the ranks).
-    strong = bool(cfg["ragged"])
+    # Strong scaling by default: one global batch of the config split over the ranks
+    # (contiguous slices of a uniform batch, token-balanced shards of the ragged one).  With
+    # --weak every rank decodes a whole batch of a uniform config.
+    strong = bool(cfg["ragged"]) or not args.weak
     if strong:
         q, kv, lens, bt, job_tokens, job_batch = make_sharded_workload(cfg, device, 1000, rank, world)
     else:
@@ -626,7 +631,11 @@ def main(argv=None):
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms = sum(step_ms) / len(step_ms)
     t = torch.tensor([ms], device=device)
+    rank_us = [ms * 1e3]
     if world > 1:
+        every = [torch.zeros(1, device=device) for _ in range(world)]
+        dist.all_gather(every, t)
+        rank_us = [float(x.item()) * 1e3 for x in every]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     gpu_launches = args.steps * (1 + (1 if splits > 1 else 0))
@@ -759,8 +768,8 @@ def main(argv=None):
         "peak": hbm if bound == "hbm" else tflops_peak,
         "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
         "frac": (achieved_gbs / hbm) if bound == "hbm" else (achieved_tf / tflops_peak),
-        "traffic": NCU_TRAFFIC.get((args.config, kname), (None, None))[0],
-        "traffic_source": NCU_TRAFFIC.get((args.config, kname), (None, "not captured for this config"))[1],
+        "traffic": None,
+        "traffic_source": "not measured by this run (DRAM bytes come from a separate ncu capture)",
         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
         "kernel": f"stage 1 ({kname})",
         "kernel_us": kern_ms * 1e3,
@@ -795,12 +804,12 @@ def main(argv=None):
                    + (", FP8 cache rows (656 B per token)" if args.kv_fp8 else ""),
                    "q_len": QL, "kv_cache": "fp8_e4m3_656" if args.kv_fp8 else "bf16", "batch_per_gpu": B, "global_batch": job_batch, "heads": 128,
                    "page_size": PAGE, "tokens_per_job": job_tokens,
-                   "tokens_per_gpu": total_tokens,
+                   "tokens_per_gpu": total_tokens, "us_per_rank": rank_us,
                    "num_splits": splits if plan is None else
                    f"per-request plan: {plan.num_units} units, {plan.num_slots} partial slots",
                    "kernel": kname,
                    "l2": "flushed (256 MiB write) before every timed step",
-                   "parallelism": (f"dp{world} (token-balanced request shards of one batch, own page pools)" if strong
+                   "parallelism": (f"dp{world} (request shards of one global batch, own page pools)" if strong
                                    else f"dp{world} (each rank its own batch and page pool)")},
         "roofline": roofline,
         "cpu_baseline": cpu,

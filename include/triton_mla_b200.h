@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define TMLA_ABI_VERSION 2
+#define TMLA_ABI_VERSION 3
 
 /* Return codes. */
 #define TMLA_OK 0
@@ -125,7 +125,9 @@ int tmla_decode(const TmlaDecodeParams* p, void* stream);
    GPU that loads it, until exit.  A call needing more workspace than that
    (tmla_workspace_bytes) returns TMLA_ERR_WORKSPACE; num_splits == 1 needs none.
    The first call on a device looks up the array's device address (make it
-   before any stream capture).  All calls share the array: calls that can
+   before any stream capture); the address is cached for the life of the process,
+   so after a cudaDeviceReset this entry point must not be called again.
+   TMLA_FLAG_PARTIAL_ONLY is ignored, as in tmla_decode.  All calls share the array: calls that can
    overlap on the GPU (different streams or host threads) race on it; calls on
    one stream are safe.  Allocates nothing (no cudaMalloc / cudaFree). */
 #define TMLA_NOALLOC_SCRATCH_BYTES (32u << 20)
@@ -291,14 +293,19 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream);
    16-byte aligned with row and group strides a multiple of 8 elements (else
    TMLA_ERR_MISALIGNED).  groups * ceil(n / 128) <= TMLA_LINEAR_MAX_TILES.  The workspace
    (tmla_linear_workspace_bytes, 16-byte aligned) starts with TMLA_LINEAR_MAX_TILES int32 tile
-   counters, which must be zero before its first use; every call leaves them at zero again
-   (the partial sums after them need no initial value).  After a call that set
-   TMLA_STATUS_TIMEOUT, zero the counters again: a piece that gave up was never counted.
-   Calls that may run at the same time (different streams) need separate workspaces.  With TMLA_LAYER_FLAG_PDL the weight loads may overlap the
-   preceding kernel, which must not write w. */
+   counters, which must be zero before its first use; every call leaves them at zero again,
+   also a call whose waits timed out (the partial sums after them need no initial value).
+   Calls that may run at the same time (different streams) need separate workspaces.  With
+   TMLA_LAYER_FLAG_PDL the weight loads may overlap the preceding kernel, which must not
+   write w.  Every pipeline wait of the kernel gives up after wait_ns nanoseconds (<= 0: 2 s):
+   the call then sets TMLA_STATUS_TIMEOUT in *status, leaves the output tiles of the CTAs that
+   gave up unwritten, and returns normally (the device stays usable).
+   TMLA_LINEAR_FLAG_TEST_STALL exists for tests of that path only: the first CTA never loads
+   its first stage, so its waits run out after wait_ns. */
 #define TMLA_W_NK 0
 #define TMLA_W_KN 1
 #define TMLA_LINEAR_MAX_TILES 65536
+#define TMLA_LINEAR_FLAG_TEST_STALL 0x100
 typedef struct TmlaLinearParams {
   const void* x;                   /* [m, k] per group */
   int64_t x_stride;
@@ -316,6 +323,7 @@ typedef struct TmlaLinearParams {
   int32_t groups;                  /* >= 1 */
   int32_t w_layout;                /* TMLA_W_NK or TMLA_W_KN */
   int64_t x_group_stride, w_group_stride, y_group_stride;  /* elements; used when groups > 1 */
+  int64_t wait_ns;                 /* limit of each pipeline wait (<= 0: 2 s) */
 } TmlaLinearParams;
 int tmla_linear(const TmlaLinearParams* p, void* stream);
 /* Workspace bytes tmla_linear needs for this shape and SM count, or -TMLA_ERR_INVALID_ARG.

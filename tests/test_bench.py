@@ -51,6 +51,25 @@ def test_sharded_workload_partitions_the_global_batch():
     assert total == job_tokens
 
 
+def test_uniform_config_is_split_over_the_ranks():
+    """Strong scaling of config 2: the global batch of 32 requests x 4096 tokens is cut into
+    equal contiguous slices, each rank holding only its own requests' pages."""
+    cpu = torch.device("cpu")
+    cfg = dict(bench.CONFIGS["cfg2"], seqlen=256)  # config 2's batch, short requests
+    for world in (1, 2, 4, 8):
+        total, rows = 0, 0
+        for rank in range(world):
+            q, kv, lens, bt, job_tokens, job_batch = bench.make_sharded_workload(cfg, cpu, 1000, rank, world)
+            assert q.shape == (32 // world, 128, 576) and kv.shape[0] == (32 // world) * 4
+            assert sorted(bt.flatten().tolist()) == list(range(kv.shape[0])), "a rank-local pool, every page once"
+            total += int(lens.sum())
+            rows += q.shape[0]
+        assert job_batch == 32 and rows == 32 and total == job_tokens == 32 * 256
+    # config 3's four requests over eight ranks: four ranks hold none
+    q, kv, lens, bt, _, _ = bench.make_sharded_workload(dict(bench.CONFIGS["cfg3"], seqlen=128), cpu, 1000, 7, 8)
+    assert q.shape[0] == 0 and lens.numel() == 0
+
+
 def test_reference_arm_prints_one_json_line():
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "3"],
                        capture_output=True, text=True, timeout=600, cwd=ROOT)

@@ -24,6 +24,21 @@ def test_library_exports_every_header_symbol():
         assert hasattr(lib, name), name
 
 
+def test_library_exports_nothing_the_header_does_not_declare():
+    """The other direction: every tmla_ function the library exports is in the header."""
+    import shutil
+    import subprocess
+
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm (binutils) not available")
+    out = subprocess.run([nm, "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.split()[-1].startswith("tmla")}
+    declared = set(re.findall(r"\b(tmla_[a-z_0-9]+)\s*\(", HEADER.read_text()))
+    assert exported == declared, exported ^ declared
+
+
 def test_abi_version_and_struct_layout():
     lib = _lib.load()
     assert lib.tmla_abi_version() == _lib.ABI_VERSION
@@ -244,9 +259,20 @@ def test_linear_workspace_bytes(m, n, k, sms, groups):
 
 def test_linear_workspace_bytes_rejects_bad_shapes():
     lib = _lib.load()
-    for args in [(0, 8, 8, 1, 148), (65, 8, 8, 1, 148), (4, 0, 8, 1, 148), (4, 8, 0, 1, 148), (4, 8, 8, 1, 0),
-                 (4, 8, 8, 0, 148)]:
+    for args in [(0, 8, 8, 1, 148), (65, 8, 8, 1, 148), (4, 0, 8, 1, 148), (4, 8, 0, 1, 148), (4, 8, 8, 0, 148)]:
         assert lib.tmla_linear_workspace_bytes(*args) == -_lib.ERR_INVALID_ARG
+
+
+def test_linear_workspace_bytes_default_sm_count():
+    """num_sms <= 0 means the current device's SM count, in the size query as in the launch;
+    without a device the query reports the CUDA error instead of a size."""
+    lib = _lib.load()
+    got = lib.tmla_linear_workspace_bytes(16, 2112, 7168, 1, 0)
+    if torch.cuda.is_available():
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        assert got == lib.tmla_linear_workspace_bytes(16, 2112, 7168, 1, sms) > 0
+    else:
+        assert got == -_lib.ERR_CUDA and lib.tmla_last_cuda_error()
 
 
 def _linear_params(**kw):

@@ -238,6 +238,85 @@ def test_bad_page_id_is_flagged_not_faulted(device):
     assert np.abs(out.float().cpu().numpy() - ref_out).max() <= OUT_TOL
 
 
+def _oracle_without_pages(case, bad):
+    """The oracle over each request's tokens minus those in the block-table slots ``bad[b]``
+    (the masked tokens of a block table whose entries there lie outside the pool)."""
+    q = case["q"].float().numpy()
+    kv = case["kv"].float().numpy()
+    page = kv.shape[1]
+    outs, lses, lens = [], [], []
+    for b in range(q.shape[0]):
+        n = int(case["seqlens"][b])
+        rows = []
+        for slot in range(-(-n // page)):
+            take = min(page, n - slot * page)
+            if slot not in bad.get(b, ()):
+                rows.append(kv[int(case["block_table"][b, slot])][:take])
+        rows = np.concatenate(rows) if rows else np.zeros((0, kv.shape[-1]), np.float32)
+        o, l = orc.mla_decode_ref(q[b:b + 1], rows[None], np.array([rows.shape[0]]), None,
+                                  softmax_scale=case["scale"])
+        outs.append(o)
+        lses.append(l)
+        lens.append(rows.shape[0])
+    return np.concatenate(outs), np.concatenate(lses), lens
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("page_size", [16, 64])
+@pytest.mark.parametrize("num_splits", [1, 2])
+def test_bad_page_ids_are_masked_on_both_kernels(device, monkeypatch, kernel, page_size, num_splits):
+    """A block-table entry outside the pool (too large or negative) masks its page's tokens
+    and sets the status bit, on the tcgen05 kernel as on the CUDA-core kernel; with 16-token
+    pages a bad page masks part of a 64-token tile, and a whole tile of bad pages leaves the
+    request with fewer tokens (or none)."""
+    import triton_mla.kernel as tk
+    monkeypatch.setattr(tk, "_CHECK", False)
+    case = recipes.paged_case([300, 130, 200, 64], 128, page_size, seed=43)
+    per_tile = 64 // page_size
+    bad = {0: {1, 3}, 1: {0}, 3: set(range(per_tile))}  # request 3: its only tile is all bad
+    bt = case["block_table"].clone()
+    for b, slots in bad.items():
+        for k, slot in enumerate(sorted(slots)):
+            bt[b, slot] = 10_000_000 if k % 2 == 0 else -5
+    case = dict(case, block_table=bt)
+    c = to_dev(case, device)
+    read_status(device)
+    out, lse = mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          num_splits=num_splits, return_lse=True, kernel=kernel)
+    torch.cuda.synchronize()
+    if kernel == "auto":
+        assert selected_kernel(c["q"], c["kv"], c["block_table"], num_splits=num_splits) == "sm100"
+    assert read_status(device) & _lib.STATUS_BAD_PAGE
+    ref_out, ref_lse, lens = _oracle_without_pages(case, bad)
+    check(out, lse, ref_out, ref_lse, lens)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("scale", [-0.1, 0.0, -(192 ** -0.5), 0.5])
+@pytest.mark.parametrize("num_splits", [1, 3])
+def test_softmax_scale_of_any_sign(device, kernel, scale, num_splits):
+    """The reference takes any softmax_scale (kernel.py:247-248): zero gives the mean of the
+    rows, a negative scale weights the smallest scores most."""
+    case = dict(recipes.paged_case([0, 1, 513, 1000], 128, 64, seed=44), scale=scale)
+    out, lse = run(case, device, num_splits=num_splits, kernel=kernel)
+    ref_out, ref_lse = oracle_of(case)
+    check(out, lse, ref_out, ref_lse, case["seqlens"])
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("num_splits", [1, 3])
+def test_nan_softmax_scale_gives_nan(device, kernel, num_splits):
+    """A NaN scale makes every score NaN: the reference returns NaN rows (and NaN LSE) for
+    requests with tokens, and 0 / -inf for empty ones."""
+    case = dict(recipes.paged_case([0, 1, 513, 1000], 128, 64, seed=45), scale=float("nan"))
+    out, lse = run(case, device, num_splits=num_splits, kernel=kernel)
+    ref_out, ref_lse = oracle_of(case)
+    out, lse = out.float().cpu().numpy(), lse.cpu().numpy()
+    assert np.isnan(ref_out[1:]).all() and np.isnan(ref_lse[1:]).all()
+    assert np.isnan(out[1:]).all() and np.isnan(lse[1:]).all()
+    assert np.all(out[0] == 0) and np.all(np.isneginf(lse[0]))
+
+
 # ----------------------------------------------------------------------------- properties at full size
 def _baseline_case(cfg, device, seed=0):
     """BASELINE configs 2-4 drawn directly on the device (values N(0,1), shuffled pages)."""
@@ -262,21 +341,24 @@ def _baseline_case(cfg, device, seed=0):
 
 
 @pytest.mark.parametrize("cfg", ["cfg2", "cfg3", "cfg4"])
-def test_baseline_configs_against_oracle_sample(device, cfg):
-    """Full-size BASELINE configs; the oracle checks a sample of requests (all of cfg2/cfg3's heads)."""
+def test_baseline_configs_against_oracle(device, cfg):
+    """Full-size BASELINE configs against the oracle: every request of configs 2 and 3 (all
+    heads), and 32 requests of config 4 (the longest, the shortest and a seeded sample)."""
     q, kv, lens, bt = _baseline_case(cfg, device)
     scale = 192 ** -0.5
     out, lse = mla_decode(q, kv, lens, bt, softmax_scale=scale, return_lse=True)
-    sample = {"cfg2": [0, 13, 31], "cfg3": [0, 3], "cfg4": [0, 7, 100, 255]}[cfg]
-    kv_np = None
+    if cfg == "cfg4":
+        order = torch.argsort(lens.cpu(), descending=True).tolist()
+        rng = np.random.default_rng(4)
+        sample = sorted(set(order[:8] + order[-8:] + rng.choice(len(order), 16, replace=False).tolist()))
+    else:
+        sample = range(len(lens))
     for b in sample:
         n = int(lens[b])
         pages = bt[b, : (n + 63) // 64].long()
         rows = kv[pages].reshape(-1, 576)[:n].float().cpu().numpy()
-        if kv_np is None:
-            kv_np = True
         ref_out, ref_lse = orc.mla_decode_ref(q[b:b + 1].float().cpu().numpy(), rows[None], np.array([n]), None,
-                                              softmax_scale=scale)
+                                              softmax_scale=scale, dtype=np.float32)
         check(out[b:b + 1], lse[b:b + 1], ref_out, ref_lse, [n])
 
 

@@ -126,3 +126,47 @@ def test_grouped_linear_matches_per_group_matmul(device, layout, m, n, k, groups
     bound = ref.abs() * 2.0 ** -8 + 1e-4 * float(ref.abs().max())
     assert not bool((err > bound).any()), f"max excess {float((err - bound).max()):.3e}"
     assert read_status(device) == 0
+
+
+def test_timed_out_wait_returns_cleanly_and_heals_the_workspace(device):
+    """A bounded wait that runs out (the test-only stall: the first CTA never loads its first
+    stage, a barrier that nothing completes) sets TMLA_STATUS_TIMEOUT and the kernel returns:
+    the call reports success, the device stays usable, the tile counters end at zero, the tiles
+    of the CTAs that finished are right and the stalled CTA's tile is left unwritten.  The next
+    call on the same workspace is exact."""
+    import ctypes
+
+    from triton_mla import _lib
+    from triton_mla.kernel import _status_word
+
+    g = torch.Generator(device=device).manual_seed(11)
+    m, n, k = 16, 2112, 7168  # 17 tiles x 56 k-steps over 148 CTAs: tile 0 is cut between CTAs 0 and 1
+    x = torch.randn(m, k, generator=g, device=device).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    lib = _lib.load()
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    ws = torch.zeros(int(lib.tmla_linear_workspace_bytes(m, n, k, 1, sms)), dtype=torch.uint8, device=device)
+    counters = ws[: 4 * _lib.LINEAR_MAX_TILES].view(torch.int32)
+    status = _status_word(device)
+    read_status(device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+    def call(y, flags, wait_ns):
+        p = _lib.TmlaLinearParams(x.data_ptr(), k, w.data_ptr(), k, y.data_ptr(), n, m, n, k, _lib.DTYPE_BF16,
+                                  ws.data_ptr(), ws.numel(), sms, flags, status.data_ptr(), 1, _lib.W_NK, 0, 0, 0,
+                                  wait_ns)
+        return lib.tmla_linear(ctypes.byref(p), stream)
+
+    y = torch.full((m, n), float("nan"), device=device, dtype=torch.bfloat16)
+    assert call(y, _lib.LINEAR_FLAG_TEST_STALL, 20_000_000) == 0
+    torch.cuda.synchronize()
+    assert read_status(device) & _lib.STATUS_TIMEOUT
+    assert int(counters.abs().sum()) == 0, "every tile counter back at zero after the timeout"
+    assert bool(torch.isnan(y[:, :128].float()).all()), "the stalled CTA's tile is not written"
+    _check(y[:, 128:], x, w[128:])
+    y2 = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+    assert call(y2, 0, 0) == 0
+    torch.cuda.synchronize()
+    assert read_status(device) == 0
+    _check(y2, x, w)
+    assert int(counters.abs().sum()) == 0

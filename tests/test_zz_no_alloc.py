@@ -73,3 +73,23 @@ def test_noalloc_matches_tmla_decode_on_consecutive_calls(device):
                                         case["seqlens"].numpy(), case["block_table"].numpy(),
                                         softmax_scale=case["scale"])
         assert np.abs(out.float().cpu().numpy() - o_np).max() <= OUT_TOL
+
+
+@pytest.mark.gpu
+def test_noalloc_ignores_the_partial_only_flag(device):
+    """With one split and TMLA_FLAG_PARTIAL_ONLY set, the call still decodes whole (the flag
+    is stage-1 semantics, which tmla_decode ignores too) instead of asking for a workspace."""
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    case = recipes.paged_case([300, 64], 128, 64, seed=6)
+    q, kv, sl, bt = (case[k].to(device) for k in ("q", "kv", "seqlens", "block_table"))
+    out = torch.empty(2, 128, 512, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(2, 128, dtype=torch.float32, device=device)
+    ref_out, ref_lse = torch.empty_like(out), torch.empty_like(lse)
+    p_ref = _params(q, kv, sl, bt, ref_out, ref_lse, 1, case["scale"])
+    p = _params(q, kv, sl, bt, out, lse, 1, case["scale"])
+    p_ref.flags = p.flags = _lib.FLAG_PARTIAL_ONLY
+    assert lib.tmla_decode(ctypes.byref(p_ref), stream) == 0
+    assert lib.tmla_decode_noalloc(ctypes.byref(p), stream) == 0
+    torch.cuda.synchronize(device)
+    assert torch.equal(out, ref_out) and torch.equal(lse, ref_lse)

@@ -29,14 +29,17 @@ int launch_combine_slots(const float* ws_o, const float* ws_lse, const int32_t* 
 }  // namespace tmla
 
 namespace {
-
 thread_local char g_cuda_error[256] = "";
+}  // namespace
 
-int cuda_fail(int neg_code) {
-  cudaError_t e = (cudaError_t)(-neg_code);
+int tmla::record_cuda_error(cudaError_t e) {
   snprintf(g_cuda_error, sizeof(g_cuda_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
   return TMLA_ERR_CUDA;
 }
+
+namespace {
+
+int cuda_fail(int neg_code) { return tmla::record_cuda_error((cudaError_t)(-neg_code)); }
 
 // Launch helpers return 0, a positive TMLA_ERR_* code or minus a cudaError_t.
 int finish(int rc) { return rc < 0 ? cuda_fail(rc) : rc; }

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 4)
   const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
   T* dst = out + (int64_t)b * osb + (int64_t)h * osh + grp * 128 + 4 * lane;
   store4<T>(dst, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
-  if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+  if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum <= 0.f ? -INFINITY : (m + log2f(wsum)) * kLn2;
 }
 
 // One warp merges one output row of d_v = 512 (the DeepSeek shape): lane l owns the float4
@@ -160,7 +160,7 @@ __device__ __forceinline__ void merge_row512(const float* __restrict__ O, int64_
 #pragma unroll
   for (int c = 0; c < 4; ++c)
     store4<T>(dst + 4 * (lane + 32 * c), make_float4(acc[c].x * inv, acc[c].y * inv, acc[c].z * inv, acc[c].w * inv));
-  if (lse_dst && lane == 0) *lse_dst = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+  if (lse_dst && lane == 0) *lse_dst = wsum <= 0.f ? -INFINITY : (m + log2f(wsum)) * kLn2;
 }
 
 constexpr int kRowWarps = 4;  // rows per CTA of the d_v = 512 merges (8 CTAs, 1024 threads per SM)
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 4)
   const float inv = wsum > 0.f ? 1.f / wsum : 1.f;
   T* dst = out + (int64_t)b * osb + (int64_t)h * osh + grp * 128 + 4 * lane;
   store4<T>(dst, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
-  if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+  if (lse && grp == 0 && lane == 0) lse[(int64_t)b * lsb + h] = wsum <= 0.f ? -INFINITY : (m + log2f(wsum)) * kLn2;
 }
 
 // General path (any d_v, any split count): one warp per row, serial over splits.
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 4)
     for (int s = 0; s < S; ++s) a = fmaf(exp2f(L[s] - m), O[(int64_t)s * DV + d], a);
     dst[d] = cvt1<T>(a * inv);
   }
-  if (lse && lane == 0) lse[(int64_t)b * lsb + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+  if (lse && lane == 0) lse[(int64_t)b * lsb + h] = wsum <= 0.f ? -INFINITY : (m + log2f(wsum)) * kLn2;
 }
 
 template <typename T>

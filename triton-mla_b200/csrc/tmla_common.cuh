@@ -62,6 +62,10 @@ __device__ __forceinline__ void split_range(int len, int num_splits, int s, int&
   end = min(start + per * 64, len);
 }
 
+// Records the name of a failed CUDA call for tmla_last_cuda_error() (per host thread) and
+// returns TMLA_ERR_CUDA: every C entry point reports CUDA failures this way.
+int record_cuda_error(cudaError_t e);
+
 // The projection kernel behind tmla_linear, for the library's own callers too: with
 // tile_aligned every CTA takes whole 128-row tiles (no partial sums, no workspace).
 int linear_launch(const TmlaLinearParams& p, bool tile_aligned, cudaStream_t stream);

@@ -209,7 +209,8 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float m_old = m_s[h];
-      const float m_new = fmaxf(m_old, mx);
+      // A row of NaN scores (a NaN scale) stays NaN, as in the reference; fmaxf would drop it.
+      const float m_new = mx != mx ? mx : fmaxf(m_old, mx);
       const bool none = m_new == -INFINITY;  // every token so far masked for this row
       const float p0 = none ? 0.f : exp2f(s0 - m_new), p1 = none ? 0.f : exp2f(s1 - m_new);
       float sum = p0 + p1;
@@ -260,7 +261,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
     if (hh >= H) break;
     const float l = l_s[h];
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    const float lse2 = l > 0.f ? m_s[h] + log2f(l) : -INFINITY;
+    const float lse2 = l <= 0.f ? -INFINITY : m_s[h] + log2f(l);  // NaN stays NaN
     if (final_out) {
       T* o = static_cast<T*>(p.out) + (int64_t)b * p.out_stride_b + (int64_t)hh * p.out_stride_h;
 #pragma unroll
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
         const int d = tid + j * kGenThreads;
         if (d < DV) o[d] = st_f<T>(acc[h][j] * inv);
       }
-      if (p.lse && tid == 0) p.lse[(int64_t)b * p.lse_stride_b + hh] = l > 0.f ? lse2 * kLn2 : -INFINITY;
+      if (p.lse && tid == 0) p.lse[(int64_t)b * p.lse_stride_b + hh] = lse2 * kLn2;
     } else {
       const int64_t row = ((int64_t)b * H + hh) * S + split;
       float* o = p.ws_o + row * DV;

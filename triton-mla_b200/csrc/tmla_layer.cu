@@ -597,7 +597,7 @@ cudaError_t launch(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 
 int finish_launch() {
   const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TMLA_OK : -(int)e;
+  return e == cudaSuccess ? TMLA_OK : tmla::record_cuda_error(e);
 }
 
 bool valid_dtype(int dt) { return dt == TMLA_DTYPE_BF16 || dt == TMLA_DTYPE_FP16 || dt == TMLA_DTYPE_FP32; }

@@ -124,25 +124,15 @@ struct Args {
   int* counters;     // [groups * n_tiles], zero between launches
   float* partials;   // [groups * n_tiles][max_parts][tokens_mma][128]
   int* status;
+  unsigned long long wait_ns;  // limit of each wait
+  int stall;         // test only: CTA 0 never loads its first stage
 };
 
-// Per-CTA %globaltimer stamps of the kernel's phases (off unless built with
-// -DTMLA_LIN_SPANS), read back with tmla_lin_span_copy().
-#ifdef TMLA_LIN_SPANS
-__device__ unsigned long long g_lin_span[1024 * 8];
-#define LIN_SPAN(k)                                                        \
-  do {                                                                     \
-    if (blockIdx.x < 1024) g_lin_span[blockIdx.x * 8 + (k)] = globaltimer(); \
-  } while (0)
-#else
-#define LIN_SPAN(k) \
-  do {              \
-  } while (0)
-#endif
-
+// A wait that gives up after `limit_ns` or as soon as another role of the CTA gave up.
 struct Waiter {
   volatile int* abort_flag;
   int* status;
+  uint64_t limit_ns;
   __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity) const {
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
@@ -152,7 +142,7 @@ struct Waiter {
         const uint64_t now = globaltimer();
         if (t0 == 0) {
           t0 = now;
-        } else if (now - t0 > kWaitNs) {
+        } else if (now - t0 > limit_ns) {
           *abort_flag = 1;
           if (status) atomicOr(status, TMLA_STATUS_TIMEOUT);
           return false;
@@ -162,11 +152,17 @@ struct Waiter {
   }
 };
 
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for drains on the way out (no abort shortcut).
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity) && globaltimer() - t0 < kWaitNs) {
+  while (!mbar_try_wait(bar, parity) && globaltimer() - t0 < limit_ns) {
   }
 }
+
+// Tile counters count the finished pieces of a cut tile in their low 16 bits and the
+// pieces that gave up (a timed-out wait) in the high bits.  The piece that completes the
+// count resets the counter to zero, and writes y only when no piece gave up.
+constexpr int kPoisoned = 1 << 16;
 
 // The weight boxes of unit (tile = group * n_tiles + t, k-step ks): per 64 columns j, 128
 // rows x 64 columns at dst + j * kWBoxBytes, K-major ([n][k] storage: one box) or MN-major
@@ -246,7 +242,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* seg_ok = reinterpret_cast<volatile int*>(bar_gen + 8 * kNumBars + 16);  // [2]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) LIN_SPAN(0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(bar(kBarFull + s), 1);
@@ -270,8 +265,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const Waiter waiter{abort_flag, a.status};
-  if (threadIdx.x == 0) LIN_SPAN(1);
+  const Waiter waiter{abort_flag, a.status, a.wait_ns};
+  // Test only: CTA 0's first stage is never loaded, so the waits for it run out.
+  const long long stalled = (a.stall && blockIdx.x == 0) ? 0 : -1;
   // Tile-aligned ranges (no tile is cut, so no partial sums), or equal unit ranges.
   const long long tiles = a.units / a.k_steps;
   const long long u0 = a.tile_aligned ? a.k_steps * unit_begin(blockIdx.x, tiles, a.grid)
@@ -290,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pre = (int)(n_units < a.stages ? n_units : a.stages);
       const int early = pre < TMLA_LIN_EARLY ? pre : TMLA_LIN_EARLY;
       for (int i = 0; i < early; ++i) {
+        if (i == stalled) continue;
         const long long u = u0 + i;
         const int tile = (int)(u / a.k_steps), ks = (int)(u - (long long)tile * a.k_steps);
         const uint32_t st = base + (uint32_t)(i * a.stage_bytes);
@@ -298,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       griddep_wait();
       griddep_launch_dependents();
-      LIN_SPAN(2);
       for (int i = 0; i < pre; ++i) {
+        if (i == stalled) continue;
         const long long u = u0 + i;
         const int tile = (int)(u / a.k_steps), ks = (int)(u - (long long)tile * a.k_steps);
         const uint32_t st = base + (uint32_t)(i * a.stage_bytes);
@@ -328,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Let the copies already in flight land before the CTA can exit.
         const long long first = issued > a.stages ? issued - a.stages : 0;
         for (long long i = first; i < issued; ++i)
-          drain_wait(bar(kBarFull + (int)(i % a.stages)), (uint32_t)(i / a.stages) & 1);
+          if (i != stalled) drain_wait(bar(kBarFull + (int)(i % a.stages)), (uint32_t)(i / a.stages) & 1, a.wait_ns);
       }
     }
   } else if (warp == 1) {
@@ -352,7 +349,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = (int)(i % a.stages);
           ok = waiter.wait(bar(kBarFull + s), (uint32_t)(i / a.stages) & 1);
           if (!ok) break;
-          if (i == 0) LIN_SPAN(3);
           tc_fence_after();
           const uint32_t st = base + (uint32_t)(s * a.stage_bytes);
 #pragma unroll
@@ -375,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok && issued_any) {
         mma_commit(bar(kBarMmaDone));
-        drain_wait(bar(kBarMmaDone), 0);
+        drain_wait(bar(kBarMmaDone), 0, a.wait_ns);
       }
     }
   } else {
@@ -384,10 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     griddep_wait();
     T* y = static_cast<T*>(a.y);
-    if (row == 0) LIN_SPAN(5);
     Segments seg{u0, u1, a.k_steps};
     int t, ka, kb;
     int acc_iter = 0;
+    bool gave_up = false;
     while (seg.next(t, ka, kb)) {
       const int buf = acc_iter & 1;
       // One thread waits and the verdict is shared, so that all 128 threads leave
@@ -395,8 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // slots: slot (i & 1) is rewritten only after every thread passed barrier i + 1.
       if (row == 0) seg_ok[buf] = waiter.wait(bar(kBarAccFull + buf), (uint32_t)(acc_iter >> 1) & 1) ? 1 : 0;
       named_sync(1, kEpiThreads);
-      if (!seg_ok[buf]) break;
-      if (row == 0 && acc_iter == 0) LIN_SPAN(4);
+      if (!seg_ok[buf]) {
+        gave_up = true;
+        break;
+      }
       tc_fence_after();
       float v[kTok];
 #pragma unroll
@@ -431,7 +429,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int m = 0; m < kTok; ++m) mine[m * kTileN + row] = v[m];
       __threadfence();
       named_sync(1, kEpiThreads);
-      if (row == 0) *last_flag = (atomicAdd(a.counters + t, 1) == parts - 1) ? 1 : 0;
+      if (row == 0) {
+        const int total = atomicAdd(a.counters + t, 1) + 1;
+        const bool last = (total & (kPoisoned - 1)) == parts;
+        if (last && total >= kPoisoned) a.counters[t] = 0;  // a piece gave up: y stays unwritten
+        *last_flag = (last && total < kPoisoned) ? 1 : 0;
+      }
       named_sync(1, kEpiThreads);
       // Read before the next segment's barrier, after which the flag may be rewritten.
       if (!*last_flag) continue;
@@ -465,7 +468,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (row == 0) a.counters[t] = 0;
     }
-    if (row == 0) LIN_SPAN(6);
+    // After a timed-out wait the rest of this CTA's pieces of cut tiles (the one whose wait
+    // gave up included) are counted as given up, so that every counter ends at zero.
+    if (gave_up && row == 0) {
+      do {
+        const long long tile_u0 = (long long)t * a.k_steps;
+        const int parts = a.tile_aligned ? 1 : unit_owner(tile_u0 + a.k_steps - 1, a.units, a.grid) -
+                                                  unit_owner(tile_u0, a.units, a.grid) + 1;
+        if (parts > 1) {
+          const int total = atomicAdd(a.counters + t, 1 + kPoisoned) + 1 + kPoisoned;
+          if ((total & (kPoisoned - 1)) == parts) a.counters[t] = 0;
+        }
+      } while (seg.next(t, ka, kb));
+    }
   }
 
   tc_fence_before();
@@ -474,7 +489,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-  if (threadIdx.x == 0) LIN_SPAN(7);
 }
 
 // ---------------------------------------------------------------------------- host side
@@ -559,7 +573,9 @@ extern "C" {
 
 int64_t tmla_linear_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t groups, int32_t num_sms) {
   tmla::linear::Plan pl;
-  if (!tmla::linear::make_plan(m, n, k, groups, num_sms, false, pl)) return -TMLA_ERR_INVALID_ARG;
+  const int sms = tmla::linear::sm_count(num_sms);  // <= 0: the current device's SM count
+  if (sms < 1) return -tmla::record_cuda_error(cudaGetLastError());
+  if (!tmla::linear::make_plan(m, n, k, groups, sms, false, pl)) return -TMLA_ERR_INVALID_ARG;
   return (int64_t)(pl.counter_bytes + pl.partial_bytes);
 }
 
@@ -587,7 +603,7 @@ int linear_launch(const TmlaLinearParams& pr, bool tile_aligned, cudaStream_t s)
       (p->groups > 1 && (p->x_group_stride % 8 || p->w_group_stride % 8)))
     return TMLA_ERR_MISALIGNED;
   const int sms = sm_count(p->num_sms);
-  if (sms < 1) return TMLA_ERR_CUDA;
+  if (sms < 1) return record_cuda_error(cudaGetLastError());
   Plan pl;
   if (!make_plan(p->m, p->n, p->k, p->groups, sms, tile_aligned, pl)) return TMLA_ERR_INVALID_ARG;
   if (!tile_aligned && (!p->workspace || p->workspace_bytes < (int64_t)(pl.counter_bytes + pl.partial_bytes) ||
@@ -628,6 +644,8 @@ int linear_launch(const TmlaLinearParams& pr, bool tile_aligned, cudaStream_t s)
   a.counters = tile_aligned ? nullptr : static_cast<int*>(p->workspace);
   a.partials = tile_aligned ? nullptr : reinterpret_cast<float*>(static_cast<char*>(p->workspace) + pl.counter_bytes);
   a.status = p->status;
+  a.wait_ns = p->wait_ns > 0 ? (unsigned long long)p->wait_ns : kWaitNs;
+  a.stall = (p->flags & TMLA_LINEAR_FLAG_TEST_STALL) ? 1 : 0;
   const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
   cudaError_t e;
   const bool half = p->dtype == TMLA_DTYPE_FP16;
@@ -646,13 +664,7 @@ int linear_launch(const TmlaLinearParams& pr, bool tile_aligned, cudaStream_t s)
       break;
   }
   if (e == cudaSuccess) e = cudaGetLastError();
-  return e == cudaSuccess ? TMLA_OK : -(int)e;
+  return e == cudaSuccess ? TMLA_OK : record_cuda_error(e);
 }
 
 }  // namespace tmla
-
-#ifdef TMLA_LIN_SPANS
-extern "C" int tmla_lin_span_copy(void* dst) {
-  return (int)cudaMemcpyFromSymbol(dst, tmla::linear::g_lin_span, sizeof(tmla::linear::g_lin_span));
-}
-#endif

@@ -17,7 +17,9 @@
 //    before touching the GPU.  A call with num_splits == 1 uses no scratch.
 //  * The array's device address is looked up once per device, by the first call
 //    made with that device current (cudaGetSymbolAddress); make that first call
-//    before any stream capture.
+//    before any stream capture.  The address is kept for the life of the process:
+//    after a cudaDeviceReset the cached address is stale, so do not call this entry
+//    point again in a process that reset its device.
 //  * All calls share the one array, so calls that can overlap on the GPU (on
 //    different streams or from different host threads) race on it.  Calls on
 //    one stream run in order and are safe.
@@ -59,6 +61,9 @@ extern "C" int tmla_decode_noalloc(const TmlaDecodeParams* p, void* stream) {
   TmlaDecodeParams q = *p;
   q.ws_o = nullptr;
   q.ws_lse = nullptr;
+  // A whole decode: as in tmla_decode, the stage-1-only flag does not apply (and with one
+  // split it would ask for a workspace this call does not attach).
+  q.flags &= ~TMLA_FLAG_PARTIAL_ONLY;
   const size_t need = tmla_workspace_bytes(q.batch, q.num_heads, q.num_splits, q.d_v);
   if (need > kScratchBytes) return TMLA_ERR_WORKSPACE;
   if (need > 0) {

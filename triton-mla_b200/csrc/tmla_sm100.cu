@@ -75,37 +75,6 @@
 namespace tmla {
 namespace sm100 {
 
-// Timeline instrumentation (off unless built with -DTMLA_TRACE_ENABLED): %globaltimer
-// stamps of pipeline events of the first CTA, read back with tmla_trace_copy().
-#ifdef TMLA_TRACE_ENABLED
-__device__ unsigned long long g_trace[16 * 256];
-#define TMLA_TRACE_IF(cond, k, j)                                                                         \
-  do {                                                                                                    \
-    if (tracing && (cond) && lane == 0 && (j) < 256) g_trace[(k) * 256 + (j)] = clock64();                 \
-  } while (0)
-#else
-#define TMLA_TRACE_IF(cond, k, j) \
-  do {                            \
-  } while (0)
-#endif
-#define TMLA_TRACE(k, j) TMLA_TRACE_IF(true, k, j)
-
-// Per-CTA %globaltimer stamps of the phases of the kernel (off unless built with
-// -DTMLA_SPAN_ENABLED), read back with tmla_span_copy().
-#ifdef TMLA_SPAN_ENABLED
-constexpr int kSpanCtas = 4096;
-__device__ unsigned long long g_span[kSpanCtas * 8];
-#define TMLA_SPAN(k)                                                                                     \
-  do {                                                                                                   \
-    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);                \
-    if (cta_ < kSpanCtas) g_span[cta_ * 8 + (k)] = globaltimer();                                        \
-  } while (0)
-#else
-#define TMLA_SPAN(k) \
-  do {               \
-  } while (0)
-#endif
-
 using namespace ptx;
 
 constexpr int kTile = 64;                 // tokens per pipeline stage
@@ -151,6 +120,7 @@ constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 36;
 constexpr uint32_t kOffMisc = kOffBar + ((kNumBars * 8 + 63) / 64) * 64;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory layout exceeds the 227 KB per-CTA limit");
+static_assert(16 + 4 * kStages <= 64, "the misc area holds the abort flag, the TMEM address and the stage masks");
 
 constexpr uint32_t kColO = 0;
 constexpr uint32_t kColQ = 256;   // Q latent dims [0, 256) of the half: 128 columns
@@ -285,14 +255,16 @@ __device__ __forceinline__ void rescale_rows16(uint32_t lanes, float alpha_a, fl
   tc_wait_st();
 }
 
-// Tokens past the end of the split may hold anything (even NaN); P is 0 there
-// but 0 * NaN is NaN, so their V rows are zeroed before PV reads the stage.
-// Called by the 128 softmax threads (thread index t in [0, 128)).
-__device__ __forceinline__ void zero_tail_rows(unsigned char* stage, int nvalid, int t) {
-  const int nrows = kTile - nvalid;
-  for (int i = t; i < nrows * 4 * 8; i += 128) {
-    const int r = nvalid + i / 32, box = (i / 8) & 3, chunk = i & 7;
-    *reinterpret_cast<uint4*>(stage + box * kBoxBytes + r * 128 + chunk * 16) = make_uint4(0, 0, 0, 0);
+// Masked tokens (past the end of the split, or in a sub-box whose page id was outside
+// the pool and was not loaded) may hold anything in shared memory, even NaN; P is 0 there
+// but 0 * NaN is NaN, so their V rows are zeroed before PV reads the stage.  Row r is
+// masked when r >= nvalid or bit r >> g_log2 of `bad` is set.  Called by the 128 softmax
+// threads (thread index t in [0, 128)).
+__device__ __forceinline__ void zero_masked_rows(unsigned char* stage, int nvalid, uint32_t bad, int g_log2, int t) {
+  for (int i = t; i < kTile * 4 * 8; i += 128) {
+    const int r = i / 32, box = (i / 8) & 3, chunk = i & 7;
+    if (r >= nvalid || ((bad >> (r >> g_log2)) & 1u))
+      *reinterpret_cast<uint4*>(stage + box * kBoxBytes + r * 128 + chunk * 16) = make_uint4(0, 0, 0, 0);
   }
   fence_proxy_async_smem();
 }
@@ -357,6 +329,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   unsigned char* smem_gen = smem_raw + (sh.base - smem_u32(smem_raw));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_gen + kOffMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_gen + kOffMisc + 8);
+  // Per ring stage: the sub-boxes of its tile whose page id was outside the pool.
+  volatile uint32_t* bad_mask = reinterpret_cast<volatile uint32_t*>(smem_gen + kOffMisc + 16);
   const uint32_t tmem_slot_addr = sh.base + kOffMisc + 8;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -380,12 +354,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool final_out = args.units ? nsplit == 1 : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
   const int H = p.num_heads;
   Waiter waiter{abort_flag, p.status};
-#ifdef TMLA_TRACE_ENABLED
-  const bool tracing = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-  if (tracing && threadIdx.x == 0) g_trace[15 * 256] = clock64();
-#endif
 
-  if (threadIdx.x == 0) TMLA_SPAN(0);
   // The request length, the block-table entries of the split and this CTA's Q rows are
   // requested before the set-up below, so that their latency overlaps it.
   const int len_req = __ldg(p.seqlens + b);
@@ -397,6 +366,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     len_in = max(0, len_req - (p.q_len - 1 - h0 / (H / p.q_len)));
   const int g = args.rows_per_load;  // token rows per TMA box
   const int nsub = kTile / g;
+  const int g_log2 = __ffs(g) - 1;
   // The producer reads the page ids of its first tile as if the request filled its table:
   // the first tile of a split then does not wait for the length and the table one after
   // the other (when the guess is wrong they are read again once the length is known).
@@ -485,35 +455,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // and the first cache tile are requested before the CTA-wide and cluster-wide syncs.
   const uint64_t pol_stream = policy_evict_first();
   // Raw page id of sub-box `sb` of tile `j` (0 when the sub-box is past the end of
-  // the split); read ahead of use, checked by `page_ok` when used.
+  // the split); read ahead of use, checked against the pool when used.
+  const int64_t npages = p.block_table ? p.num_pages : (int64_t)p.batch;
   auto page_of = [&](int j, int sb) -> int {
     const int t = start + j * kTile + sb * g;
     if (sb >= nsub || t >= end || j >= ntiles) return 0;
     if (!p.block_table) return b;
     return __ldg(p.block_table + (int64_t)b * p.bt_stride + t / p.page_size);
   };
-  // Whether sub-box `sb` of tile `j` is inside the split; a page id outside the
-  // pool is reported and replaced by page 0 (its tokens are not trusted).
-  auto page_ok = [&](int j, int sb, int& pg) -> bool {
-    const int t = start + j * kTile + sb * g;
-    if (sb >= nsub || t >= end || j >= ntiles) return false;
-    if (pg < 0 || (int64_t)pg >= (int64_t)(p.block_table ? p.num_pages : p.batch)) {
-      if (p.status) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
-      pg = 0;
-    }
-    return true;
-  };
   // Loads of tile j (ring stage j % kStages, RoPE slot j % kRopeSlots) once both are free.
+  // Lane l loads sub-box l.  A page id outside the pool is reported and its sub-box is not
+  // loaded: the stage's mask word records it, and the softmax masks those tokens (score
+  // -inf, V rows zeroed), as the CUDA-core kernel does.
   auto issue_tile = [&](int j, int pg) {
     const int s = j % kStages, rs = j % kRopeSlots;
-    const int t0 = start + j * kTile;
-    const int live = min(nsub, (end - t0 + g - 1) / g);
-    if (lane == 0) mbar_arrive_expect_tx(sh.bar(kBarKvFull + s), (uint32_t)(live * g) * kRowBytes);
-    TMLA_TRACE(0, j);
-    if (lane == 0 && j == 0) TMLA_SPAN(2);
+    const int t = start + j * kTile + lane * g;
+    const bool live = lane < nsub && t < end;
+    const bool bad = live && (pg < 0 || (int64_t)pg >= npages);
+    const uint32_t loads = __ballot_sync(0xffffffffu, live && !bad);
+    const uint32_t bads = __ballot_sync(0xffffffffu, bad);
+    if (bads && lane == 0 && p.status) atomicOr(p.status, TMLA_STATUS_BAD_PAGE);
+    if (lane == 0) {
+      bad_mask[s] = bads;
+      mbar_arrive_expect_tx(sh.bar(kBarKvFull + s), (uint32_t)(__popc(loads) * g) * kRowBytes);
+    }
     __syncwarp();
-    if (page_ok(j, lane, pg)) {
-      const int t = t0 + lane * g;
+    if (live && !bad) {
       const int slot = p.block_table ? t % p.page_size : t;
       const uint32_t dst = sh.stage(s);
       const uint32_t bar = sh.bar(kBarKvFull + s);
@@ -544,7 +511,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // the peer's barriers are initialised before any remote arrive / st.async
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) TMLA_SPAN(1);
 
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------ TMA producer, part 2
@@ -582,8 +548,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!waiter.wait(sh.bar(kBarKvFull + s), (j / kStages) & 1)) break;
         // Score buffer sb was last read for tile j-2.
         if (j >= 2 && !waiter.wait(sh.bar(kBarSEmpty0 + sb), ((j - 2) >> 1) & 1)) break;
-        TMLA_TRACE(1, j);
-        if (j == 0) TMLA_SPAN(3);
         tc_fence_after();
         const uint32_t st = sh.stage(s), rp = sh.rope(j % kRopeSlots);
         const uint32_t d = tmem + kColS + 64 * sb;
@@ -614,8 +578,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < ntiles; ++j) {
         const int pb = j & 1;
         if (!waiter.wait(sh.bar(kBarPFull0 + pb), (j >> 1) & 1)) break;
-        TMLA_TRACE(2, j);
-        if (j == ntiles - 1) TMLA_SPAN(4);
         tc_fence_after();
         const uint32_t st = sh.stage(j % kStages), pbuf = sh.base + kOffPBuf + (j % kPBufs) * kPBufBytes;
 #pragma unroll
@@ -728,7 +690,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        TMLA_TRACE_IF(quarter == 0, 3, j);
         tc_fence_after();
         float s[32];
         {
@@ -760,7 +721,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        TMLA_TRACE_IF(quarter == 0, 4, j);
         uint32_t dep = 0;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -776,31 +736,64 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // issue while a load of this warp is still in flight (a warp's loads complete for
         // all lanes at once).
         if (lane == 0) mbar_arrive(after_loads(sh.bar(kBarSinRead0 + ib), dep));
-        TMLA_TRACE_IF(quarter == 0, 5, j);
 
         // Online softmax (base 2) with lazy rescaling; a row's 64 scores sit in 4 threads.
-        // Maxima are taken on the unscaled scores (softmax_scale > 0) and the scale is
-        // folded into the exponent's FMA; only a partial last tile needs masking.
+        // The scale is folded into the exponent's FMA, so the row maximum of the scaled
+        // scores is the largest raw score times the scale for a positive scale and the
+        // smallest for a negative one.  Only a tile with masked tokens (the last one of the
+        // split, or one with a page id outside the pool) needs masking.
+        const float sc = args.scale_log2;
+        const bool neg = sc < 0.f;
         const int nvalid = min(kTile, end - (start + j * kTile));
-        if (nvalid < kTile) {
+        uint32_t bm = 0;
+        if (p.block_table) {
+          // The producer wrote the stage's mask before arming its barrier (already complete).
+          if (!waiter.wait(sh.bar(kBarKvFull + j % kStages), (uint32_t)(j / kStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          bm = bad_mask[j % kStages];
+        }
+        const bool partial = nvalid < kTile || bm != 0u;
+        if (partial) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int col = 8 * (i >> 2) + 2 * t4 + (i & 1);
-            if (col >= nvalid) s[i] = -INFINITY;
+            if (col >= nvalid || ((bm >> (col >> g_log2)) & 1u)) s[i] = neg ? INFINITY : -INFINITY;
           }
         }
-        float mx_a = -INFINITY, mx_b = -INFINITY;
+        float mx_a, mx_b;
+        if (!neg) {
+          mx_a = mx_b = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i & 2)
-            mx_b = fmaxf(mx_b, s[i]);
-          else
-            mx_a = fmaxf(mx_a, s[i]);
+          for (int i = 0; i < 32; ++i) {
+            if (i & 2)
+              mx_b = fmaxf(mx_b, s[i]);
+            else
+              mx_a = fmaxf(mx_a, s[i]);
+          }
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        } else {
+          mx_a = mx_b = INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i & 2)
+              mx_b = fminf(mx_b, s[i]);
+            else
+              mx_a = fminf(mx_a, s[i]);
+          }
+          mx_a = fminf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+          mx_b = fminf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+          mx_a = fminf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+          mx_b = fminf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
         }
-        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2)) * args.scale_log2;
-        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2)) * args.scale_log2;
+        // A row whose tokens are all masked in this tile has no maximum here (and a zero
+        // scale must not turn the infinite mask value into NaN).
+        mx_a = isinf(mx_a) ? -INFINITY : mx_a * sc;
+        mx_b = isinf(mx_b) ? -INFINITY : mx_b * sc;
         if (kSinBufs == 2 && j > 0 && !take_running_max()) {
           ok = false;
           break;
@@ -830,9 +823,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         float sum_a = 0.f, sum_b = 0.f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float sc = args.scale_log2;
-          const float p0 = ex2(fmaf(s[4 * k], sc, -mn_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -mn_a));
-          const float p2 = ex2(fmaf(s[4 * k + 2], sc, -mn_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -mn_b));
+          float p0 = ex2(fmaf(s[4 * k], sc, -mn_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -mn_a));
+          float p2 = ex2(fmaf(s[4 * k + 2], sc, -mn_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -mn_b));
+          if (partial) {
+            // Masked tokens weigh exactly 0, also when the row has no maximum yet.
+            const int c0 = 8 * k + 2 * t4;
+            const bool v0 = c0 < nvalid && !((bm >> (c0 >> g_log2)) & 1u);
+            const bool v1 = c0 + 1 < nvalid && !((bm >> ((c0 + 1) >> g_log2)) & 1u);
+            p0 = v0 ? p0 : 0.f;
+            p2 = v0 ? p2 : 0.f;
+            p1 = v1 ? p1 : 0.f;
+            p3 = v1 ? p3 : 0.f;
+          }
           sum_a += p0 + p1;
           sum_b += p2 + p3;
           pw[2 * k] = pack2(p0, p1, kFp16);
@@ -840,7 +842,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         l_a += sum_a;
         l_b += sum_b;
-        TMLA_TRACE_IF(quarter == 0, 6, j);
         // P buffer pbi (in both CTAs) was last read by PV(j - kPBufs).
         if (j >= kPBufs && !waiter.wait(sh.bar(kBarPairPvDone0 + ((j - kPBufs) & 1)), (uint32_t)((j - kPBufs) >> 1) & 1u)) {
           ok = false;
@@ -868,7 +869,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             st_async_f2(alpha_remote + (uint32_t)sb * kAlphaBytes + (uint32_t)(quarter * 8 + L) * 8u, al_a, al_b,
                         pinfull_remote + 8u * sb);
         }
-        TMLA_TRACE_IF(quarter == 0, 7, j);
         if (j > 0 && __any_sync(0xffffffffu, need_a || need_b)) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), (uint32_t)((j - 1) >> 1) & 1u)) {
             ok = false;
@@ -877,14 +877,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           rescale_rows16(tmem + own_lanes, al_a, al_b);
         }
-        if (nvalid < kTile) zero_tail_rows(smem_gen + kOffStages + (j % kStages) * kStageBytes, nvalid, t128);
-        TMLA_TRACE_IF(quarter == 0, 8, j);
+        if (partial) zero_masked_rows(smem_gen + kOffStages + (j % kStages) * kStageBytes, nvalid, bm, g_log2, t128);
         // The peer's rows of P(j) and their rescale factors.
         if (!waiter.wait(sh.bar(kBarPinFull0 + sb), ph, true)) {
           ok = false;
           break;
         }
-        TMLA_TRACE_IF(quarter == 0, 11, j);
         const float2 al = alpha_in[sb * 32 + quarter * 8 + L];
         if (__any_sync(0xffffffffu, j > 0 && (al.x != 1.f || al.y != 1.f))) {
           if (!waiter.wait(sh.bar(kBarPvDone0 + ((j - 1) & 1)), (uint32_t)((j - 1) >> 1) & 1u)) {
@@ -897,7 +895,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sh.bar(kBarPFull0 + sb));
-        TMLA_TRACE_IF(quarter == 0, 12, j);
       }
       // Row sums: add the four threads' shares; both warpgroups' (l, m) meet in shared memory.
       l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
@@ -928,9 +925,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           lstat[2 * row] = l;
           const int hh = h0 + row;
           if (hh < H) {
-            const float lse2 = l > 0.f ? mf + log2f(l) : -INFINITY;
+            // An empty row gives -inf; a NaN sum (a NaN scale or input) stays NaN.
+            const float lse2 = l <= 0.f ? -INFINITY : mf + log2f(l);
             if (final_out) {
-              if (p.lse) p.lse[(int64_t)b * p.lse_stride_b + hh] = l > 0.f ? lse2 * kLn2 : -INFINITY;
+              if (p.lse) p.lse[(int64_t)b * p.lse_stride_b + hh] = lse2 * kLn2;
             } else if (args.units) {
               p.ws_lse[(int64_t)slot * H + hh] = lse2;
             } else {
@@ -955,7 +953,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
         tc_fence_after();
       }
-      if (wg == 0 && quarter == 0 && lane == 0) TMLA_SPAN(5);
       const float l = lstat[2 * (quarter * 32 + lane)];
       stage_rows<T>(smem_gen + kOffStages, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
                     4 * wg, 4, final_out);
@@ -984,7 +981,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           bulk_commit_group();
           bulk_wait_group0();
         }
-        TMLA_SPAN(6);
       }
     } else {
       // ---------------------------------------------------------- score sender for the peer's 16 rows
@@ -993,7 +989,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < ntiles; ++j) {
         const int sb = j & 1;
         if (!waiter.wait(sh.bar(kBarSFull0 + sb), (j >> 1) & 1)) break;
-        TMLA_TRACE_IF(quarter == 0, 9, j);
         tc_fence_after();
         uint32_t r[32];
         tmem_ld16x256_x8(tmem + peer_lanes + kColS + 64 * sb, r);
@@ -1008,7 +1003,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 8; ++c)
           st_async_u4(sin_remote + (uint32_t)ib * kSinBytes + (uint32_t)((quarter * 8 + c) * 32 + lane) * 16u,
                       make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]), sinfull_remote + 8u * ib);
-        TMLA_TRACE_IF(quarter == 0, 10, j);
       }
     }
   }
@@ -1023,7 +1017,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-  if (threadIdx.x == 0) TMLA_SPAN(7);
 }
 
 // ---------------------------------------------------------------------------- host side
@@ -1168,14 +1161,3 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
 }
 
 }  // namespace tmla
-
-#ifdef TMLA_SPAN_ENABLED
-extern "C" int tmla_span_copy(void* dst) {
-  return (int)cudaMemcpyFromSymbol(dst, tmla::sm100::g_span, sizeof(tmla::sm100::g_span));
-}
-#endif
-#ifdef TMLA_TRACE_ENABLED
-extern "C" int tmla_trace_copy(void* dst) {
-  return (int)cudaMemcpyFromSymbol(dst, tmla::sm100::g_trace, sizeof(tmla::sm100::g_trace));
-}
-#endif

@@ -15,7 +15,7 @@ from pathlib import Path
 LIB_NAME = "libtriton_mla_b200.so"
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 OK = 0
 ERR_INVALID_ARG = 1
@@ -24,6 +24,8 @@ ERR_MISALIGNED = 3
 ERR_CUDA = 4
 ERR_WORKSPACE = 5
 LAYER_FLAG_PDL = 1
+LINEAR_FLAG_TEST_STALL = 0x100
+LINEAR_MAX_TILES = 65536
 W_NK = 0
 W_KN = 1
 KV_SAME = 0
@@ -210,6 +212,7 @@ class TmlaLinearParams(ctypes.Structure):
         ("x_group_stride", ctypes.c_int64),
         ("w_group_stride", ctypes.c_int64),
         ("y_group_stride", ctypes.c_int64),
+        ("wait_ns", ctypes.c_int64),
     ]
 
 
