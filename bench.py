@@ -23,7 +23,8 @@ cached tokens, weights replicated on every rank).
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 numpy oracle) on the host cores on a bounded sample of the same workload.
 ``--impl cutlass-mla`` times a library kernel (vLLM's CUTLASS sm100 MLA decode)
-on the same workload, one GPU, for comparison.
+on the same workload, one GPU, for comparison; ``--impl reference-gpu`` times the
+reference's own Triton kernel (installed unmodified in baseline/_ref) the same way.
 """
 
 from __future__ import annotations
@@ -445,6 +446,85 @@ def run_reference(args):
     return 0
 
 
+REFERENCE_GPU_SCRIPT = r"""
+import json, sys, time
+sys.path.insert(0, {root!r})
+import bench
+sys.path[:] = [p for p in sys.path if not p.endswith("triton-mla_b200")]
+sys.path.insert(0, {ref!r})
+import numpy as np
+import torch
+import triton_mla
+from triton_mla import mla_decode
+assert triton_mla.__file__.startswith({ref!r}), triton_mla.__file__
+from oracle import mla_oracle as orc
+cfg = bench.CONFIGS[{config!r}]
+device = torch.device("cuda", 0)
+torch.cuda.set_device(device)
+q, kv, lens, bt = bench.make_workload(cfg, device, seed=1000)
+for _ in range({warmup}):
+    out = mla_decode(q, kv, lens, bt, softmax_scale=bench.SCALE)
+torch.cuda.synchronize()
+flush = torch.empty(bench.L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+stream = torch.cuda.current_stream(device)
+starts = [torch.cuda.Event(enable_timing=True) for _ in range({steps})]
+ends = [torch.cuda.Event(enable_timing=True) for _ in range({steps})]
+for i in range({steps}):
+    flush.zero_()
+    starts[i].record(stream)
+    out = mla_decode(q, kv, lens, bt, softmax_scale=bench.SCALE)
+    ends[i].record(stream)
+torch.cuda.synchronize()
+ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / {steps}
+n = int(lens[0])
+rows = kv[bt[0, : (n + 63) // 64].long()].reshape(-1, 576)[:n].float().cpu().numpy()
+ref, _ = orc.mla_decode_ref(q[:1].float().cpu().numpy(), rows[None], np.array([n]), None, softmax_scale=bench.SCALE,
+                            dtype=np.float32)
+err = float(np.abs(out[:1].float().cpu().numpy() - ref).max())
+print(json.dumps({{"ms": ms, "tokens": int(lens.sum()), "batch": int(q.shape[0]), "max_abs_err_request0": err,
+                  "triton": __import__("triton").__version__}}))
+"""
+
+
+def run_reference_gpu(args):
+    """--impl reference-gpu: the reference's own Triton ``mla_decode`` (installed unmodified into
+    baseline/_ref) on the same workload, GPU 0, for comparison.  It runs in a subprocess, since
+    the reference's package has the same import name as this repository's.  Measurement only."""
+    line = {"impl": "reference-gpu", "metric": METRIC, "n_gpus": args.gpus}
+    ref = ROOT / "baseline" / "_ref"
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    if not (ref / "triton_mla" / "kernel.py").exists():
+        line["unavailable"] = "the reference is not installed in baseline/_ref"
+        print(json.dumps(line), flush=True)
+        return 0
+    cfg = CONFIGS[args.config]
+    if cfg.get("layer"):
+        line["unavailable"] = "the reference GPU comparison covers the decode configs (cfg2-cfg4)"
+        print(json.dumps(line), flush=True)
+        return 0
+    script = REFERENCE_GPU_SCRIPT.format(root=str(ROOT), ref=str(ref), config=args.config, warmup=args.warmup,
+                                         steps=args.steps)
+    r = subprocess.run([sys.executable, "-c", script], capture_output=True, text=True, timeout=1800)
+    if r.returncode != 0:
+        line["unavailable"] = "the reference Triton kernel did not run: " + (r.stderr.strip().splitlines() or ["?"])[-1]
+        print(json.dumps(line), flush=True)
+        return 0
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    tflops = decode_flops(d["tokens"], 128) / (d["ms"] * 1e-3) / 1e12
+    line.update({
+        "value": tflops, "unit": "TFLOPS", "steps": args.steps, "warmup": args.warmup, "ms_per_step": d["ms"],
+        "us_per_call": d["ms"] * 1e3, "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1)",
+        "config": {"workload": cfg["desc"], "batch": d["batch"], "tokens": d["tokens"],
+                   "num_splits": "reference default (num_splits=None: get_num_splits, one host sync)",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "reference": f"triton_mla 0.1.1 (unmodified, baseline/_ref), triton {d['triton']}",
+        "max_abs_err_request0_vs_oracle": d["max_abs_err_request0"],
+    })
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_library(args):
     """--impl cutlass-mla: a library MLA decode kernel on the same workload, for comparison.
 
@@ -475,34 +555,42 @@ def run_library(args):
     torch.cuda.set_device(device)
     q, kv, lens, bt = make_workload(cfg, device, seed=1000)
     B = q.shape[0]
-    if bt.shape[1] % 2:  # the library reads 128-token tiles: an even number of 64-token pages per row
+    ours = mla_decode(q, kv, lens, bt, softmax_scale=SCALE)
+    # The library's kernel works on 128-token tiles.  It is timed on the same 64-token pages
+    # as this repository's arm (an even number of pages per block-table row), and on a copy
+    # of the same tokens in 128-token pages (consecutive page pairs of each request), the
+    # page size its fast path reads with TMA.
+    if bt.shape[1] % 2:
         bt = torch.cat([bt, bt[:, :1]], dim=1).contiguous()
+    kv128 = kv[bt.long()].reshape(B, -1, 2 * PAGE, D_QK).reshape(-1, 2 * PAGE, D_QK).contiguous()
+    bt128 = torch.arange(kv128.shape[0], device=device, dtype=torch.int32).view(B, -1).contiguous()
     q_nope, q_pe = q[..., :D_V].contiguous(), q[..., D_V:].contiguous()
     out = torch.empty(B, 128, D_V, dtype=torch.bfloat16, device=device)
     lse = torch.empty(B, 128, dtype=torch.float32, device=device)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     ws = torch.empty(max(vops.sm100_cutlass_mla_get_workspace_size(int(lens.max()), B, sms, -1), 1),
                      dtype=torch.uint8, device=device)
-
-    def step():
-        vops.sm100_cutlass_mla_decode(out, lse, q_nope, q_pe, kv, lens, bt, ws, SCALE, -1)
-
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
-    for _ in range(args.warmup):
-        step()
-    ours = mla_decode(q, kv, lens, bt, softmax_scale=SCALE)
-    torch.cuda.synchronize()
-    diff = float((out.float() - ours.float()).abs().max())
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for i in range(args.steps):
-        flush.zero_()
-        starts[i].record(stream)
-        step()
-        ends[i].record(stream)
-    torch.cuda.synchronize()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    results = {}
+    for name, cache, table in (("page64", kv, bt), ("page128", kv128, bt128)):
+        def step():
+            vops.sm100_cutlass_mla_decode(out, lse, q_nope, q_pe, cache, lens, table, ws, SCALE, -1)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        diff = float((out.float() - ours.float()).abs().max())
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        results[name] = (sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps, diff)
+    ms, diff = min(results.values())
     total_tokens = int(lens.sum())
     tflops = decode_flops(total_tokens, 128) / (ms * 1e-3) / 1e12
     import vllm
@@ -513,6 +601,8 @@ def run_library(args):
                    "l2": "flushed (256 MiB write) before every timed step"},
         "library": f"vllm {vllm.__version__} torch.ops._C.sm100_cutlass_mla_decode",
         "max_abs_diff_vs_mla_decode": diff,
+        "us_per_call_by_page_size": {k: v[0] * 1e3 for k, v in results.items()},
+        "max_abs_diff_by_page_size": {k: v[1] for k, v in results.items()},
     })
     print(json.dumps(line), flush=True)
     return 0
@@ -524,7 +614,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "cutlass-mla"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu", "cutlass-mla"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "sm100", "generic"])
     ap.add_argument("--kv-fp8", action="store_true",
                     help="an FP8 cache (656-byte rows, triton_mla.fp8_cache; CUDA-core kernel)")
@@ -541,6 +631,8 @@ def main(argv=None):
         return run_reference(args)
     if args.impl == "cutlass-mla":
         return run_library(args)
+    if args.impl == "reference-gpu":
+        return run_reference_gpu(args)
 
     import torch
     import torch.distributed as dist

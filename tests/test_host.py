@@ -313,3 +313,29 @@ def test_linear_helpers_refuse_cpu_tensors():
     assert not layer_ops.linear_ok(x, w) and not layer_ops.linear_preferred(x, w)
     with pytest.raises(AssertionError):
         layer_ops.linear(x, w)
+
+
+def test_split_rule_restated_for_torch_compile_matches_the_library():
+    from triton_mla.kernel import _num_splits_rule
+    lib = _lib.load()
+    for b in (1, 2, 3, 4, 16, 32, 64, 256, 1024):
+        for h in (16, 128, 256):
+            for s in (1, 64, 100, 4096, 16384, 65536):
+                for sms in (132, 148):
+                    assert _num_splits_rule(b, h, s, sms) == lib.tmla_num_splits(b, h, s, sms), (b, h, s, sms)
+
+
+def test_decode_is_a_registered_torch_operator_with_a_meta_kernel():
+    """torch.ops.triton_mla.decode exists with the documented schema, and its Meta kernel
+    accepts meta tensors (what torch.compile's tracing runs)."""
+    op = torch.ops.triton_mla.decode
+    schema = str(op.default._schema)
+    assert "Tensor(a!) out" in schema and "Tensor(b!) lse" in schema and "int num_splits" in schema
+    meta = torch.device("meta")
+    q = torch.empty(4, 128, 576, dtype=torch.bfloat16, device=meta)
+    kv = torch.empty(64, 64, 576, dtype=torch.bfloat16, device=meta)
+    lens = torch.empty(4, dtype=torch.int32, device=meta)
+    bt = torch.empty(4, 16, dtype=torch.int32, device=meta)
+    out = torch.empty(4, 128, 512, dtype=torch.bfloat16, device=meta)
+    lse = torch.empty(4, 128, dtype=torch.float32, device=meta)
+    op(q, kv, lens, bt, out, lse, 2, 0.07, 0, 1, None)

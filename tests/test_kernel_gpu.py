@@ -735,3 +735,27 @@ def test_fp8_cache_with_several_query_tokens(device):
         check(out[:, i], lse[:, i], ref_out[:, i], ref_lse[:, i], tok_lens[:, i])
     with pytest.raises(_lib.LibraryError):
         mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], kernel="sm100")
+
+
+def test_torch_compile_fullgraph_through_the_operator(device):
+    """mla_decode is one operator (torch.ops.triton_mla.decode), so torch.compile traces a
+    function that calls it, with an explicit split count, into one graph without a break;
+    the compiled function matches the oracle."""
+    import torch._dynamo
+
+    case = recipes.paged_case([0, 1, 513, 1000], 128, 64, seed=46)
+    c = to_dev(case, device)
+    scale = c["scale"]
+
+    def f(q, kv, lens, bt):
+        out, lse = mla_decode(q, kv, lens, bt, softmax_scale=scale, num_splits=3, return_lse=True)
+        return out.float() * 2.0, lse
+
+    torch._dynamo.reset()
+    explain = torch._dynamo.explain(f)(c["q"], c["kv"], c["seqlens"], c["block_table"])
+    assert explain.graph_break_count == 0 and explain.graph_count == 1, explain.break_reasons
+    compiled = torch.compile(f, fullgraph=True, backend="aot_eager")
+    out2, lse = compiled(c["q"], c["kv"], c["seqlens"], c["block_table"])
+    ref_out, ref_lse = oracle_of(case)
+    check(out2 / 2.0, lse, ref_out, ref_lse, case["seqlens"])
+    torch._dynamo.reset()

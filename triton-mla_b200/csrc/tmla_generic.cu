@@ -49,7 +49,7 @@ __host__ __device__ inline int gen_row_pad(int d) { return d + 8; }
 __host__ __device__ inline int gen_q_pad(int d) { return d + 4; }
 
 size_t generic_smem_bytes(int d_qk, int elt) {
-  size_t f = (size_t)kGenHeads * gen_q_pad(d_qk) + kGenHeads * kGenTok + 3 * kGenHeads;
+  size_t f = (size_t)kGenHeads * gen_q_pad(d_qk) + kGenHeads * kGenTok + 3 * kGenHeads + kGenTok;
   return f * 4 + (size_t)kGenTok * gen_row_pad(d_qk) * elt + 16;
 }
 
@@ -94,9 +94,10 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
   float* m_s = p_s + kGenHeads * kGenTok;            // running max (base 2)
   float* l_s = m_s + kGenHeads;                      // running sum
   float* a_s = l_s + kGenHeads;                      // per-tile rescale factor
+  int* bad_s = reinterpret_cast<int*>(a_s + kGenHeads);  // [32]: the row's page id is outside the pool
   // FP8 rows are dequantised to fp32 (a 16-bit tile would round the scaled values again).
   using KT = typename std::conditional<kFp8Cache, float, T>::type;
-  KT* k_s = reinterpret_cast<KT*>(a_s + kGenHeads);  // [32][Dk]
+  KT* k_s = reinterpret_cast<KT*>(bad_s + kGenTok);  // [32][Dk]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int h0 = blockIdx.x * kGenHeads, split = blockIdx.y, b = blockIdx.z;
@@ -135,6 +136,17 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
 
   constexpr int VE = Vec<T>::kPerChunk;
   for (int t0 = start; t0 < end; t0 += kGenTok) {
+    // Tokens behind a block-table entry outside the pool are masked out of the softmax (their
+    // rows below are zeros); the row loads report them in the status word.
+    if (tid < kGenTok) {
+      const int tok = t0 + tid, slot = tok / p.page_size;
+      int bad = 0;
+      if (p.block_table && tok < end) {
+        const int page = slot < p.bt_width ? p.block_table[(int64_t)b * p.bt_stride + slot] : -1;
+        bad = page < 0 || (int64_t)page >= p.num_pages;
+      }
+      bad_s[tid] = bad;
+    }
     // Stage the tile's cache rows (zeros past `end` or behind a bad page id).
     if constexpr (kFp8Cache) {
       // 656-byte rows: 64 words of 8 latent e4m3 values (scaled by the row's 4 fp32 scales)
@@ -195,7 +207,7 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
         const KT* kr = k_s + r * Dk;
         float s = 0.f;
         for (int d = 0; d < D; ++d) s = fmaf(qr[d], ld_f<KT>(kr + d), s);
-        p_s[h * kGenTok + r] = (t0 + r < row_end) ? s : -INFINITY;
+        p_s[h * kGenTok + r] = (t0 + r < row_end && !bad_s[r]) ? s : -INFINITY;
       }
     }
     __syncthreads();
@@ -206,8 +218,13 @@ __global__ void __launch_bounds__(kGenThreads) mla_generic_split_kernel(TmlaDeco
       const int r = lane & 15;
       float s0 = p_s[h * kGenTok + r], s1 = p_s[h * kGenTok + r + 16];
       float mx = fmaxf(s0, s1);
+      int nan = (s0 != s0) || (s1 != s1);
 #pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      for (int o = 8; o >= 1; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+      }
+      if (nan) mx = __int_as_float(0x7fc00000);  // fmaxf drops NaN scores; keep them
       const float m_old = m_s[h];
       // A row of NaN scores (a NaN scale) stays NaN, as in the reference; fmaxf would drop it.
       const float m_new = mx != mx ? mx : fmaxf(m_old, mx);

@@ -916,9 +916,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int o = quarter * 16 + lane;
           const float2 A = wst[o], Bw = wst[64 + o];
           const float mf = fmaxf(A.y, Bw.y);
+          // A warpgroup whose maximum never left -inf has a zero sum, or NaN (a NaN scale),
+          // which must reach the LSE.
           float l = 0.f;
-          if (A.y != -INFINITY) l += A.x * ex2(A.y - mf);
-          if (Bw.y != -INFINITY) l += Bw.x * ex2(Bw.y - mf);
+          l += A.y != -INFINITY ? A.x * ex2(A.y - mf) : (A.x != A.x ? A.x : 0.f);
+          l += Bw.y != -INFINITY ? Bw.x * ex2(Bw.y - mf) : (Bw.x != Bw.x ? Bw.x : 0.f);
           const int row = quarter * 32 + 16 * (int)rank + lane;
           st_async_f2(map_to_rank(sh.base + kOffFin, peer) + (uint32_t)o * 8u, l, mf,
                       map_to_rank(sh.bar(kBarFinFull), peer));

@@ -288,6 +288,25 @@ def load() -> ctypes.CDLL:
     return lib
 
 
+TORCH_OP_PATH = Path(__file__).resolve().parent / "libtriton_mla_torch.so"
+_torch_op_loaded = False
+
+
+def load_torch_op():
+    """Register ``torch.ops.triton_mla.decode`` (the decode as a PyTorch operator, over the C
+    ABI); returns the operator.  Raises ImportError when its library is missing."""
+    global _torch_op_loaded
+    import torch
+
+    if not _torch_op_loaded:
+        if not TORCH_OP_PATH.exists():
+            raise ImportError(f"{TORCH_OP_PATH} is missing: build it with `python triton-mla_b200/build.py`")
+        load()  # the C library first: the operator library links against it
+        torch.ops.load_library(str(TORCH_OP_PATH))
+        _torch_op_loaded = True
+    return torch.ops.triton_mla.decode
+
+
 def error_string(code: int) -> str:
     return load().tmla_error_string(code).decode()
 

@@ -146,6 +146,24 @@ def make_split_plan(cache_seqlens, num_heads: int, device=None) -> SplitPlan:
     return SplitPlan(units, req_first, device)
 
 
+def _num_splits_rule(batch, num_heads, max_seqlen, num_sms):
+    """``tmla_num_splits`` restated for torch.compile, which cannot trace the ctypes call (the
+    same estimate: waves x (rows per split + fixed rows) + merge traffic, smallest count within
+    2% of the best)."""
+    if batch <= 0 or num_heads <= 0 or max_seqlen <= 0:
+        return 1
+    clusters = max(num_sms // 2, 1)
+    units = batch * ((num_heads + 127) // 128)
+    tiles = (max_seqlen + 63) // 64
+    merge = batch * num_heads * 512.0 * 8.0 / (clusters * 1152.0)
+    cost = {}
+    for s in range(1, min(tiles, 64) + 1):
+        waves = (units * s + clusters - 1) // clusters
+        cost[s] = waves * (((tiles + s - 1) // s) * 64.0 + 256.0) + (merge * s if s > 1 else 0.0)
+    best = min(cost.values())
+    return next(s for s in sorted(cost) if cost[s] <= best * 1.02)
+
+
 def get_num_splits(batch, num_heads, max_seqlen, num_sms, min_tokens_per_split=128):
     """Split count for one decode call on B200.
 
@@ -191,6 +209,7 @@ def read_status(device=None, reset: bool = True) -> int:
 
 
 _CHECK = os.environ.get("TRITON_MLA_CHECK", "0") == "1"
+_DECODE_OP = _lib.load_torch_op()
 
 
 def _require_cuda(*tensors):
@@ -306,9 +325,15 @@ def mla_decode(
         bt_stride = 0
 
     device = q.device
+    compiling = torch.compiler.is_compiling()
     if plan is not None:
         assert plan.batch == batch, "the split plan was made for another batch size"
         num_splits = 1
+    elif num_splits is None and compiling:
+        # Under torch.compile the split count comes from the host-side rule on the longest
+        # request the cache can hold (no sync on the lengths, no graph break).
+        max_seqlen = bt_width * page_size if paged else kv_cache.shape[1]
+        num_splits = _num_splits_rule(batch, num_heads, max_seqlen, _num_sms(device))
     elif num_splits is None:
         if batch > 0 and torch.cuda.is_current_stream_capturing():
             # No host sync during capture.  The tcgen05 kernel follows a plan made on the GPU
@@ -356,14 +381,21 @@ def mla_decode(
     if batch == 0:
         return _shaped(out, lse)
 
+    if plan is None:
+        # One operator call: torch.ops.triton_mla.decode (C ABI tmla_decode underneath), on the
+        # current stream, workspace from the caching allocator.
+        _DECODE_OP(q, kv_cache, cache_seqlens, block_table, out, lse, num_splits, float(softmax_scale),
+                   _KERNELS[kernel], q_len, None if compiling else _status_word(device))
+        if _CHECK and not compiling and not torch.cuda.is_current_stream_capturing():
+            st = read_status(device)
+            if st:
+                raise RuntimeError(f"mla_decode device status 0x{st:x} (bad page id / length, or a wait timed out)")
+        return _shaped(out, lse)
+
     lib = _lib.load()
-    if plan is not None:
-        slots = plan.num_slots
-        ws_bytes = lib.tmla_units_workspace_bytes(slots, num_heads, head_dim_v)
-        o_bytes = (slots * num_heads * head_dim_v * 4 + 255) & ~255
-    else:
-        ws_bytes = lib.tmla_workspace_bytes(batch, num_heads, num_splits, head_dim_v)
-        o_bytes = (batch * num_heads * num_splits * head_dim_v * 4 + 255) & ~255
+    slots = plan.num_slots
+    ws_bytes = lib.tmla_units_workspace_bytes(slots, num_heads, head_dim_v)
+    o_bytes = (slots * num_heads * head_dim_v * 4 + 255) & ~255
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
     ws_o = ws_lse = None
     if ws is not None:
@@ -385,12 +417,9 @@ def mla_decode(
         torch.cuda.set_device(device)
     try:
         stream = torch.cuda.current_stream(device).cuda_stream
-        if plan is None:
-            _lib.check(lib.tmla_decode(ctypes.byref(p), ctypes.c_void_p(stream)), "tmla_decode")
-        else:
-            _lib.check(lib.tmla_decode_units(ctypes.byref(p), plan.units.data_ptr(), plan.req_first.data_ptr(),
-                                             plan.num_units, plan.num_slots, ctypes.c_void_p(stream)),
-                       "tmla_decode_units")
+        _lib.check(lib.tmla_decode_units(ctypes.byref(p), plan.units.data_ptr(), plan.req_first.data_ptr(),
+                                         plan.num_units, plan.num_slots, ctypes.c_void_p(stream)),
+                   "tmla_decode_units")
     finally:
         if prev != device.index:
             torch.cuda.set_device(prev)
