@@ -113,7 +113,8 @@ typedef struct TmlaDecodeParams {
 } TmlaDecodeParams;
 
 /* Whole decode: partial attention over num_splits KV ranges, then the merge.
-   Replaces `mla_decode` (kernel.py:204-323) after its host-side validation. */
+   Replaces `mla_decode` (kernel.py:204-323) after its host-side validation.
+   TMLA_FLAG_PARTIAL_ONLY is ignored (it is stage-1 semantics, tmla_decode_partial). */
 int tmla_decode(const TmlaDecodeParams* p, void* stream);
 
 /* Whole decode without any allocation.  No counterpart in the reference: it is

@@ -170,12 +170,15 @@ int tmla_combine(const float* ws_o, const float* ws_lse, void* out, int64_t out_
 }
 
 int tmla_decode(const TmlaDecodeParams* p, void* stream) {
-  int rc = validate(p);
-  if (rc) return rc;
-  if (p->batch == 0) return TMLA_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!p) return TMLA_ERR_INVALID_ARG;
+  // A whole decode: the stage-1-only flag does not apply (with one split it would ask for a
+  // workspace the call does not need).
   TmlaDecodeParams q = *p;
   q.flags &= ~TMLA_FLAG_PARTIAL_ONLY;
+  int rc = validate(&q);
+  if (rc) return rc;
+  if (q.batch == 0) return TMLA_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = run_partial(q, s);
   if (rc) return rc;
   if (p->num_splits == 1) return TMLA_OK;
