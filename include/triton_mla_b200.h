@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define TMLA_ABI_VERSION 3
+#define TMLA_ABI_VERSION 4
 
 /* Return codes. */
 #define TMLA_OK 0
@@ -59,6 +59,10 @@ extern "C" {
 
 /* Flags. */
 #define TMLA_FLAG_PARTIAL_ONLY 0x1  /* write ws_o / ws_lse even when num_splits == 1 (stage-1 semantics) */
+/* Tests of the timeout path only (tcgen05 kernel): the first cluster's first CTA never loads its
+   first cache tile, so its waits run out after wait_ns; the call sets TMLA_STATUS_TIMEOUT and
+   returns normally, with the rows of that cluster invalid. */
+#define TMLA_FLAG_TEST_STALL 0x100
 
 /* Cache row formats (TmlaDecodeParams.kv_format).
    TMLA_KV_SAME: d_qk values of the q dtype per token.
@@ -110,6 +114,10 @@ typedef struct TmlaDecodeParams {
   float softmax_scale;
   int32_t q_len;                   /* query tokens per request (0 or 1: one); divides num_heads */
   int32_t kv_format;               /* TMLA_KV_*: the cache row format */
+  /* Limit of each pipeline wait of the tcgen05 kernel in nanoseconds (<= 0: 2 s).  A wait that
+     runs out sets TMLA_STATUS_TIMEOUT; the kernel stops, lets its copies and MMAs finish and
+     returns, and the device stays usable. */
+  int64_t wait_ns;
 } TmlaDecodeParams;
 
 /* Whole decode: partial attention over num_splits KV ranges, then the merge.

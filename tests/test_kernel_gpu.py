@@ -759,3 +759,42 @@ def test_torch_compile_fullgraph_through_the_operator(device):
     ref_out, ref_lse = oracle_of(case)
     check(out2 / 2.0, lse, ref_out, ref_lse, case["seqlens"])
     torch._dynamo.reset()
+
+
+def test_decode_timed_out_wait_returns_cleanly(device):
+    """A bounded wait of the tcgen05 kernel that runs out (TMLA_FLAG_TEST_STALL: the first CTA
+    never loads its first tile, a barrier that nothing completes) sets TMLA_STATUS_TIMEOUT, and
+    the pair of CTAs stops, lets what it has in flight land and returns: the call succeeds, the
+    requests of the other clusters are right, and the next call on the same device is exact."""
+    import ctypes
+
+    from triton_mla.kernel import _status_word
+
+    case = recipes.paged_case([1024, 777, 300, 65], 128, 64, seed=47)
+    c = to_dev(case, device)
+    B, splits = 4, 2
+    lib = _lib.load()
+    out = torch.empty(B, 128, 512, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(B, 128, dtype=torch.float32, device=device)
+    ws = torch.empty(lib.tmla_workspace_bytes(B, 128, splits, 512), dtype=torch.uint8, device=device)
+    o_bytes = (B * 128 * splits * 512 * 4 + 255) & ~255
+    status = _status_word(device)
+    read_status(device)
+    bt = c["block_table"]
+    p = _lib.TmlaDecodeParams(
+        c["q"].data_ptr(), c["q"].stride(0), c["q"].stride(1), c["kv"].data_ptr(), c["kv"].stride(0),
+        c["kv"].stride(1), c["kv"].shape[0], 64, c["seqlens"].data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1],
+        out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0), ws.data_ptr(),
+        ws.data_ptr() + o_bytes, status.data_ptr(), B, 128, 576, 512, splits, _lib.DTYPE_BF16, _lib.KERNEL_SM100,
+        _lib.FLAG_TEST_STALL, case["scale"], 1, _lib.KV_SAME, 20_000_000)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    assert lib.tmla_decode(ctypes.byref(p), stream) == 0
+    torch.cuda.synchronize()
+    assert read_status(device) & _lib.STATUS_TIMEOUT
+    ref_out, ref_lse = oracle_of(case)
+    check(out[1:], lse[1:], ref_out[1:], ref_lse[1:], case["seqlens"][1:])  # request 0 held the stalled cluster
+    p.flags, p.wait_ns = 0, 0
+    assert lib.tmla_decode(ctypes.byref(p), stream) == 0
+    torch.cuda.synchronize()
+    assert read_status(device) == 0
+    check(out, lse, ref_out, ref_lse, case["seqlens"])

@@ -131,7 +131,8 @@ constexpr int kWarpQK = 1;
 constexpr int kWarpPV = 2;
 constexpr int kWarpRelay = 3;
 
-constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr uint64_t kWaitNs = 2000000000ull;   // default limit of each wait
+constexpr uint64_t kInFlightNs = 100000ull;   // how long a pair that gave up keeps its shared memory
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8 between rescales
 
 // Barrier indices.
@@ -178,10 +179,13 @@ struct Shared {
   __device__ uint32_t rope(uint32_t r) const { return base + kOffRope + r * kRopeBytes; }
 };
 
-// A wait that gives up after kWaitNs or as soon as another role gave up.
+// A wait that gives up after `limit` ns or as soon as another role of this CTA or of the
+// peer gave up; on giving up it raises the abort flag of both CTAs of the pair.
 struct Waiter {
   volatile int* abort_flag;
   int* status;
+  uint64_t limit;
+  uint32_t peer_abort;  // the peer's abort flag (shared::cluster address)
   __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, bool cluster_scope = false) const {
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
@@ -192,8 +196,9 @@ struct Waiter {
         uint64_t now = globaltimer();
         if (t0 == 0) {
           t0 = now;
-        } else if (now - t0 > kWaitNs) {
+        } else if (now - t0 > limit) {
           *abort_flag = 1;
+          asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
           if (status) atomicOr(status, TMLA_STATUS_TIMEOUT);
           return false;
         }
@@ -203,9 +208,9 @@ struct Waiter {
 };
 
 // Bounded wait for drains on the way out (no abort shortcut).
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t limit) {
   const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity) && globaltimer() - t0 < kWaitNs) {
+  while (!mbar_try_wait(bar, parity) && globaltimer() - t0 < limit) {
   }
 }
 
@@ -216,6 +221,8 @@ struct KernelArgs {
   // Per-request split plan (tmla_decode_units) or NULL: entry z = {request, split,
   // splits of that request, partial slot (-1: the request has one split)}.
   const int4* units;
+  uint64_t wait_ns;    // limit of each wait
+  int stall;           // test only: the first cluster's rank-0 CTA never loads its first tile
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool fp16) {
@@ -353,7 +360,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // One split writes the final output (and natural-log LSE); several write fp32 partials.
   const bool final_out = args.units ? nsplit == 1 : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
   const int H = p.num_heads;
-  Waiter waiter{abort_flag, p.status};
+  const Waiter waiter{abort_flag, p.status, args.wait_ns, map_to_rank(sh.base + kOffMisc, peer)};
+  // Test only (TMLA_FLAG_TEST_STALL): this CTA never loads tile 0, so the waits for it run out.
+  const bool stalled = args.stall && rank == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
 
   // The request length, the block-table entries of the split and this CTA's Q rows are
   // requested before the set-up below, so that their latency overlaps it.
@@ -397,6 +406,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
+    *reinterpret_cast<volatile int*>(smem_gen + kOffMisc + 4) = 0;
     mbar_init(sh.bar(kBarQFull), 1 + 4);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(sh.bar(kBarKvFull + s), 1);
@@ -501,7 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                   policy_evict_last());
     }
     if (ntiles > 0) {
-      issue_tile(0, start == spec_start ? pg_spec : page_of(0, lane));
+      if (!stalled) issue_tile(0, start == spec_start ? pg_spec : page_of(0, lane));
       pg_next = page_of(1, lane);
     }
   }
@@ -530,10 +540,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // Drain: every issued load (the last ring stages and Q) has landed before the CTA may exit.
     if (lane == 0) {
       for (int j = max(0, issued - kStages); j <= issued; ++j) {
-        if (j < issued)
-          drain_wait(sh.bar(kBarKvFull + j % kStages), (j / kStages) & 1);
-        else
-          drain_wait(sh.bar(kBarQFull), 0);
+        if (j < issued) {
+          if (!(stalled && j == 0)) drain_wait(sh.bar(kBarKvFull + j % kStages), (j / kStages) & 1, args.wait_ns);
+        } else {
+          drain_wait(sh.bar(kBarQFull), 0, args.wait_ns);
+        }
       }
     }
   } else if (warp == kWarpQK) {
@@ -566,7 +577,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mma_commit(sh.bar(kBarRopeEmpty + j % kRopeSlots));
       }
       mma_commit(sh.bar(kBarDrainQK));
-      drain_wait(sh.bar(kBarDrainQK), 0);
+      drain_wait(sh.bar(kBarDrainQK), 0, args.wait_ns);
     }
     __syncwarp();
   } else if (warp == kWarpPV) {
@@ -595,10 +606,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mma_commit_cluster(pairdone_remote + 8u * pb);
       }
       mma_commit(sh.bar(kBarDrainPV));
-      drain_wait(sh.bar(kBarDrainPV), 0);
+      drain_wait(sh.bar(kBarDrainPV), 0, args.wait_ns);
       // The peer's commits on this CTA's pair barriers have all landed once their last
-      // phases completed; only then may this CTA exit.
-      for (int j = max(0, ntiles - 2); j < ntiles; ++j) drain_wait(sh.bar(kBarPairPvDone0 + (j & 1)), (j >> 1) & 1);
+      // phases completed; only then may this CTA exit.  (After a timeout the teardown below
+      // waits for them instead: the peer may not have issued those PVs.)
+      if (!*abort_flag)
+        for (int j = max(0, ntiles - 2); j < ntiles; ++j)
+          drain_wait(sh.bar(kBarPairPvDone0 + (j & 1)), (j >> 1) & 1, args.wait_ns);
     }
     __syncwarp();
   } else if (warp == kWarpRelay) {
@@ -1012,9 +1026,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // The split merge, when it follows in the stream, may be scheduled once every CTA got here.
   griddep_launch_dependents();
   // Teardown: both CTAs are done with each other's shared memory before either exits.
+  // Each CTA tells the peer whether it gave up (a plain remote store, which the cluster
+  // barrier orders).  The barrier orders such stores, not the asynchronous transfers the peer
+  // issued into this CTA before reaching it (st.async score rows and rescale factors, bulk
+  // copies of P rows, MMA-commit arrivals on the pair barriers).  On the normal path this CTA
+  // waited for every one of them; after a timed-out wait it did not, so both CTAs then hold
+  // their shared memory a while longer (kInFlightNs, far above a transfer's latency) before
+  // leaving: a CTA that exits under a landing transfer loses the context.
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0)
+    asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(sh.base + kOffMisc + 4, peer)),
+                 "r"(*abort_flag ? 1 : 0)
+                 : "memory");
   cluster_sync();
+  if (threadIdx.x == 0 && (*abort_flag || *reinterpret_cast<volatile int*>(smem_gen + kOffMisc + 4))) {
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < kInFlightNs) {
+    }
+  }
   if (warp == kWarpQK) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -1134,6 +1164,8 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   a.rows_per_load = g;
   a.scale_log2 = p.softmax_scale * kLog2e;
   a.units = reinterpret_cast<const int4*>(units);
+  a.wait_ns = p.wait_ns > 0 ? (uint64_t)p.wait_ns : kWaitNs;
+  a.stall = (p.flags & TMLA_FLAG_TEST_STALL) ? 1 : 0;
   const dim3 grid(2 * ((p.num_heads + 127) / 128), units ? 1 : p.num_splits, units ? num_units : p.batch);
   // A programmatic dependent of the preceding kernel in the stream: the CTAs may be placed
   // while that kernel finishes, and every read of an input follows griddep_wait().

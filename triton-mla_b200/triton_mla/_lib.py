@@ -15,7 +15,7 @@ from pathlib import Path
 LIB_NAME = "libtriton_mla_b200.so"
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 OK = 0
 ERR_INVALID_ARG = 1
@@ -43,6 +43,7 @@ KERNEL_GENERIC = 1
 KERNEL_SM100 = 2
 
 FLAG_PARTIAL_ONLY = 0x1
+FLAG_TEST_STALL = 0x100
 
 NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -106,6 +107,7 @@ class TmlaDecodeParams(ctypes.Structure):
         ("softmax_scale", ctypes.c_float),
         ("q_len", ctypes.c_int32),
         ("kv_format", ctypes.c_int32),
+        ("wait_ns", ctypes.c_int64),
     ]
 
 
