@@ -23,7 +23,7 @@ def _close(got, ref, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("batch,heads", [(1, 16), (16, 128), (37, 20)])
+@pytest.mark.parametrize("batch,heads", [(1, 16), (16, 128), (37, 20), (80, 20)])
 @pytest.mark.parametrize("overlap", [False, True])
 def test_q_absorb_rope_matches_torch(device, dtype, batch, heads, overlap):
     g = torch.Generator(device=device).manual_seed(batch * 131 + heads)

@@ -523,6 +523,25 @@ __global__ void __launch_bounds__(128) q_absorb_rope_mma_kernel(TmlaQPrepParams 
   }
 }
 
+// RoPE half of the decode query alone: q_out[b, h, rank + k] for the d_rope values of q_pe
+// (the W_UK product goes to the projection kernel).  Grid (heads), 128 threads.
+template <typename T>
+__global__ void __launch_bounds__(128) q_rope_kernel(TmlaQPrepParams p) {
+  after_predecessor();
+  const int h = blockIdx.x, half = p.d_rope / 2;
+  const T* q_in = static_cast<const T*>(p.q_in);
+  T* q_out = static_cast<T*>(p.q_out);
+  for (int i = threadIdx.x; i < p.batch * half; i += blockDim.x) {
+    const int b = i / half, k = i % half;
+    const T* src = q_in + (int64_t)b * p.q_in_stride_b + (int64_t)h * p.q_in_stride_h + p.d_nope;
+    float oa, ob;
+    rope_pair(ld(src + k), ld(src + k + half), p.positions[b], k, p.d_rope, p.rope_theta, oa, ob);
+    T* dst = q_out + (int64_t)b * p.q_out_stride_b + (int64_t)h * p.q_out_stride_h + p.rank;
+    dst[k] = cvt<T>(oa);
+    dst[k + half] = cvt<T>(ob);
+  }
+}
+
 // o: grid (heads, d_v / 32), 128 threads.  The CTA computes 32 rows of W_UV[h] (d) x 16
 // requests; warp w owns the 16 x 8 tile (d rows 16 (w & 1) .., requests 8 (w >> 1) ..) over
 // the whole K = rank, so no partial sums cross warps.  A = W_UV rows (row-major), B = o rows
@@ -618,8 +637,42 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (p->flags & TMLA_LAYER_FLAG_PDL) != 0;
   cudaError_t e = cudaSuccess;
+  if (p->dtype != TMLA_DTYPE_FP32 && p->batch <= 64 && (uintptr_t)p->q_in % 16 == 0 && p->q_in_stride_b % 8 == 0 &&
+      p->q_in_stride_h % 8 == 0 && p->rank % 8 == 0) {
+    // Up to 64 requests of a 16-bit type: the W_UK product on the weight-streaming tcgen05
+    // kernel, one group per head (W_UK[h] is [d_nope][rank], the head's first d_nope rows of
+    // w_kv_b: a [k][n] weight), tile-aligned (no partial sums, no workspace).  The RoPE half
+    // is a separate small launch before it; the projection kernel is its programmatic
+    // dependent (it streams its weight tiles while the RoPE runs, and reads q_in after).
+    if (p->d_rope) {
+      if (p->dtype == TMLA_DTYPE_BF16)
+        e = launch(pdl, q_rope_kernel<__nv_bfloat16>, dim3(p->num_heads), dim3(128), 0, s, *p);
+      else
+        e = launch(pdl, q_rope_kernel<__half>, dim3(p->num_heads), dim3(128), 0, s, *p);
+      if (e != cudaSuccess) return tmla::record_cuda_error(e);
+    }
+    TmlaLinearParams lp = {};
+    lp.x = p->q_in;
+    lp.x_stride = p->q_in_stride_b;
+    lp.x_group_stride = p->q_in_stride_h;
+    lp.w = p->w_kv_b;
+    lp.w_stride = p->rank;
+    lp.w_group_stride = (int64_t)(p->d_nope + p->d_v) * p->rank;
+    lp.w_layout = TMLA_W_KN;
+    lp.y = p->q_out;
+    lp.y_stride = p->q_out_stride_b;
+    lp.y_group_stride = p->q_out_stride_h;
+    lp.m = p->batch;
+    lp.n = p->rank;
+    lp.k = p->d_nope;
+    lp.groups = p->num_heads;
+    lp.dtype = p->dtype;
+    lp.flags = (p->d_rope || pdl) ? TMLA_LAYER_FLAG_PDL : 0;
+    return tmla::linear_launch(lp, true, s);
+  }
   if (p->dtype != TMLA_DTYPE_FP32 && p->d_nope % 16 == 0 && p->rank % kCols == 0) {
-    // 16-bit types: the contraction on tensor cores (mma.sync m16n8k16, fp32 accumulation).
+    // 16-bit types, more than 64 requests: the contraction on tensor cores (mma.sync m16n8k16,
+    // fp32 accumulation).
     const size_t smem = ((size_t)p->d_nope * (kCols + 8) + (size_t)kBChunk * (p->d_nope + 8)) * esz;
     if (p->dtype == TMLA_DTYPE_BF16) {
       e = cudaFuncSetAttribute(q_absorb_rope_mma_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -630,7 +683,7 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream) {
                                (int)smem);
       if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_mma_kernel<__half>, grid, block, smem, s, *p);
     }
-    if (e != cudaSuccess) return -(int)e;
+    if (e != cudaSuccess) return tmla::record_cuda_error(e);
     return finish_launch();
   }
   const size_t smem = (size_t)p->d_nope * kCols * esz + (size_t)kBChunk * p->d_nope * sizeof(float);
@@ -648,7 +701,7 @@ int tmla_q_absorb_rope(const TmlaQPrepParams* p, void* stream) {
       e = cudaFuncSetAttribute(q_absorb_rope_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) e = launch(pdl, q_absorb_rope_kernel<float>, grid, block, smem, s, *p);
   }
-  if (e != cudaSuccess) return -(int)e;
+  if (e != cudaSuccess) return tmla::record_cuda_error(e);
   return finish_launch();
 }
 
@@ -674,7 +727,7 @@ int tmla_kv_norm_rope_append(const TmlaKvAppendParams* p, void* stream) {
     default:
       e = launch(pdl, kv_append_kernel<float>, grid, block, 0, s, *p);
   }
-  if (e != cudaSuccess) return -(int)e;
+  if (e != cudaSuccess) return tmla::record_cuda_error(e);
   return finish_launch();
 }
 
@@ -726,7 +779,7 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream) {
       e = cudaFuncSetAttribute(o_unabsorb_mma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) e = launch(pdl, o_unabsorb_mma_kernel<__half>, grid_mma, block, smem, s, *p);
     }
-    if (e != cudaSuccess) return -(int)e;
+    if (e != cudaSuccess) return tmla::record_cuda_error(e);
     return finish_launch();
   }
   const size_t smem = (size_t)(16 + kBChunk) * (p->rank + 8) * esz;
@@ -743,7 +796,7 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream) {
       e = cudaFuncSetAttribute(o_unabsorb_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) e = launch(pdl, o_unabsorb_kernel<float>, grid, block, smem, s, *p);
   }
-  if (e != cudaSuccess) return -(int)e;
+  if (e != cudaSuccess) return tmla::record_cuda_error(e);
   return finish_launch();
 }
 

@@ -120,7 +120,7 @@ constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 36;
 constexpr uint32_t kOffMisc = kOffBar + ((kNumBars * 8 + 63) / 64) * 64;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory layout exceeds the 227 KB per-CTA limit");
-static_assert(16 + 4 * kStages <= 64, "the misc area holds the abort flag, the TMEM address and the stage masks");
+static_assert(16 + 4 * kStages + 8 <= 64, "the misc area holds the abort flag, the TMEM address and the masks");
 
 constexpr uint32_t kColO = 0;
 constexpr uint32_t kColQ = 256;   // Q latent dims [0, 256) of the half: 128 columns
@@ -336,8 +336,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   unsigned char* smem_gen = smem_raw + (sh.base - smem_u32(smem_raw));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_gen + kOffMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_gen + kOffMisc + 8);
-  // Per ring stage: the sub-boxes of its tile whose page id was outside the pool.
+  // Per ring stage: the sub-boxes of its tile whose page id was outside the pool; per score
+  // buffer: the same mask for the tile whose scores it holds.
   volatile uint32_t* bad_mask = reinterpret_cast<volatile uint32_t*>(smem_gen + kOffMisc + 16);
+  volatile uint32_t* tile_mask = reinterpret_cast<volatile uint32_t*>(smem_gen + kOffMisc + 16 + 4 * kStages);
   const uint32_t tmem_slot_addr = sh.base + kOffMisc + 8;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -414,7 +416,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int r = 0; r < kRopeSlots; ++r) mbar_init(sh.bar(kBarRopeEmpty + r), 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(sh.bar(kBarSFull0 + i), 1);
+      mbar_init(sh.bar(kBarSFull0 + i), 2);  // the QK commit + the QK thread (tile mask published)
       mbar_init(sh.bar(kBarSEmpty0 + i), 8);
       mbar_init(sh.bar(kBarPFull0 + i), 4);
       mbar_init(sh.bar(kBarPvDone0 + i), 1);
@@ -575,6 +577,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         mma_commit(sh.bar(kBarSFull0 + sb));
         mma_commit(sh.bar(kBarRopeEmpty + j % kRopeSlots));
+        // The tile's masked sub-boxes travel with its scores: the softmax reads them after
+        // SFull, whose phase completes with this thread's arrival as well as the commit.
+        tile_mask[sb] = bad_mask[s];
+        mbar_arrive(sh.bar(kBarSFull0 + sb));
       }
       mma_commit(sh.bar(kBarDrainQK));
       drain_wait(sh.bar(kBarDrainQK), 0, args.wait_ns);
@@ -704,6 +710,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        const uint32_t bm = tile_mask[sb];  // the tile's masked sub-boxes (published with SFull)
         tc_fence_after();
         float s[32];
         {
@@ -759,15 +766,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const float sc = args.scale_log2;
         const bool neg = sc < 0.f;
         const int nvalid = min(kTile, end - (start + j * kTile));
-        uint32_t bm = 0;
-        if (p.block_table) {
-          // The producer wrote the stage's mask before arming its barrier (already complete).
-          if (!waiter.wait(sh.bar(kBarKvFull + j % kStages), (uint32_t)(j / kStages) & 1u)) {
-            ok = false;
-            break;
-          }
-          bm = bad_mask[j % kStages];
-        }
+
         const bool partial = nvalid < kTile || bm != 0u;
         if (partial) {
 #pragma unroll
