@@ -225,6 +225,12 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Copy a 128-row x 256-bit matrix (16 16-bit values per row) from shared memory, described by
+// a matrix descriptor, to TMEM: row r -> lane r, its 32 bytes -> 8 consecutive columns.  Runs
+// in order with this thread's tcgen05.mma operations.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t s_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(s_desc) : "memory");
+}
 // Arrive (once) on a CTA-local mbarrier when all prior tcgen05 ops of this thread complete.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");

@@ -93,6 +93,7 @@ constexpr uint32_t kStageBytes = 4 * kBoxBytes;               // 32768: latent b
 constexpr uint32_t kRowBytes = (kHalfLatent + kHalfRope) * 2;  // cache bytes per token per CTA (576)
 constexpr uint32_t kQBoxBytes = 128 * 128;                  // 128 heads x 64 dims, swizzled
 constexpr uint32_t kQRopeBytes = 128 * kHalfRope * 2;       // 8192
+constexpr uint32_t kQLatBytes = 4 * kQBoxBytes;             // this CTA's 256 latent dims of 128 heads
 constexpr uint32_t kSinBytes = 64 * kTile * 4;              // 16384: peer's partial S for my 64 heads
 constexpr uint32_t kPBufBytes = 128 * kTile * 2;            // 16384: P of all 128 rows, SW128 K-major
 constexpr uint32_t kPPeerBytes = 64 * kTile * 2;            // 8192: the rows of P that come from the peer
@@ -167,6 +168,7 @@ enum : uint32_t {
   kBarMaxB0 = kBarMaxA0 + 4,  // warpgroup B (odd tiles), per quarter
   kBarWgStats = kBarMaxB0 + 4,  // both warpgroups' final (l, m) are in shared memory
   kBarEpi,         // the epilogue tiles are staged (8 warps)
+  kBarQCopied,     // Q's latent half has been copied from ring stages 2-3 into TMEM
   kBarCount,
 };
 
@@ -326,6 +328,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_sm100_split_kernel(const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
                            const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_part,
                            const __grid_constant__ CUtensorMap tm_q_rope,
+                           const __grid_constant__ CUtensorMap tm_q_lat,
                            const __grid_constant__ KernelArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const TmlaDecodeParams& p = args.p;
@@ -397,19 +400,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int64_t line = max((int64_t)0, first / 32 - 8) + lane;
     if (line * 32 < p.bt_width) prefetch_l2(p.block_table + (int64_t)b * p.bt_stride + line * 32);
   }
-  if (warp >= 4 && warp < 8) {
-    const int hq = h0 + (warp - 4) * 32 + lane;
-    if (hq < H) {
-      const char* qrow = reinterpret_cast<const char*>(static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b +
-                                                       (int64_t)hq * p.q_stride_h + kHalfLatent * rank);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) prefetch_l2(qrow + 128 * c);
-    }
-  }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     *reinterpret_cast<volatile int*>(smem_gen + kOffMisc + 4) = 0;
-    mbar_init(sh.bar(kBarQFull), 1 + 4);
+    mbar_init(sh.bar(kBarQFull), 1);
+    mbar_init(sh.bar(kBarQCopied), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(sh.bar(kBarKvFull + s), 1);
       mbar_init(sh.bar(kBarKvEmpty + s), 1);
@@ -450,6 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_kv_lat);
     prefetch_tmap(&tm_kv_rope);
     prefetch_tmap(&tm_q_rope);
+    prefetch_tmap(&tm_q_lat);
   }
 
   // Token range of this split (whole 64-token tiles; see split_range).
@@ -508,9 +504,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == kWarpProducer) {
     __syncwarp();
     if (lane == 0) {
-      mbar_arrive_expect_tx(sh.bar(kBarQFull), kQRopeBytes);
+      // Q: the RoPE half into its own buffer, this CTA's 256 latent dims (four 64-dim boxes of
+      // 128 heads) into ring stages 2-3, which the QK warp copies into TMEM before its first MMA
+      // (rows past H are zero-filled).
+      mbar_arrive_expect_tx(sh.bar(kBarQFull), kQRopeBytes + kQLatBytes);
       tma_load_3d(sh.base + kOffQRope, &tm_q_rope, sh.bar(kBarQFull), 512 + kHalfRope * rank, h0, b,
                   policy_evict_last());
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tma_load_3d(sh.stage(2) + c * kQBoxBytes, &tm_q_lat, sh.bar(kBarQFull), kHalfLatent * rank + 64 * c, h0, b,
+                    policy_evict_last());
     }
     if (ntiles > 0) {
       if (!stalled) issue_tile(0, start == spec_start ? pg_spec : page_of(0, lane));
@@ -533,6 +536,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int s = j % kStages, rs = j % kRopeSlots;
       bool ok = true;
       if (lane == 0 && j >= kStages) ok = waiter.wait(sh.bar(kBarKvEmpty + s), ((j / kStages) - 1) & 1);
+      // Stages 2 and 3 first held Q's latent half, until the QK warp copied it into TMEM.
+      if (lane == 0 && ok && j == 2) ok = waiter.wait(sh.bar(kBarQCopied), 0);
       if (lane == 0 && ok && j >= kRopeSlots) ok = waiter.wait(sh.bar(kBarRopeEmpty + rs), ((j / kRopeSlots) - 1) & 1);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
@@ -556,6 +561,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t idesc = idesc_f16(fmt, 128, kTile, 0);
       const uint32_t q_rope = sh.base + kOffQRope;
       bool ok = ntiles == 0 || waiter.wait(sh.bar(kBarQFull), 0);
+      if (ok && ntiles > 0) {
+        // Q's latent half: smem (ring stages 2-3, 128B-swizzled 64-dim boxes) -> TMEM columns
+        // kColQ + 8k for the 16-dim step k, ahead of (and in order with) the first QK.
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          tmem_cp_128x256b(tmem + kColQ + 8 * k,
+                           smem_desc(sh.stage(2) + (k >> 2) * kQBoxBytes + (k & 3) * 32, 16, 1024, kSwizzle128B));
+        mma_commit(sh.bar(kBarQCopied));
+      }
       for (int j = 0; ok && j < ntiles; ++j) {
         const int s = j % kStages, sb = j & 1;
         if (!waiter.wait(sh.bar(kBarKvFull + s), (j / kStages) & 1)) break;
@@ -656,31 +671,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     if (role <= 2) {
       const int wg = role - 1;  // this warpgroup runs the tiles j with j % 2 == wg
-      if (wg == 0) {
-        // Q latent dims of this CTA's half -> TMEM, all 32 rows of the quarter (rows past H are zero).
-        const int hq = h0 + quarter * 32 + lane;
-        const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
-                        kHalfLatent * rank;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t w[32];
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            uint4 x = make_uint4(0, 0, 0, 0);
-            if (hq < H) x = __ldg(reinterpret_cast<const uint4*>(qrow + 64 * c + 8 * v));
-            w[4 * v] = x.x;
-            w[4 * v + 1] = x.y;
-            w[4 * v + 2] = x.z;
-            w[4 * v + 3] = x.w;
-          }
-          tmem_st32(tmem + q_lanes + kColQ + 32 * c, w);
-        }
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sh.bar(kBarQFull));
-      }
-
       // ---------------------------------------------------------- softmax of my 16 rows of this quarter
       // Tiles alternate between the two warpgroups.  The running maximum of tile j-1
       // comes from the other warpgroup through shared memory (one barrier per quarter);
@@ -768,16 +758,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int nvalid = min(kTile, end - (start + j * kTile));
 
         const bool partial = nvalid < kTile || bm != 0u;
-        if (partial) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = 8 * (i >> 2) + 2 * t4 + (i & 1);
-            if (col >= nvalid || ((bm >> (col >> g_log2)) & 1u)) s[i] = neg ? INFINITY : -INFINITY;
-          }
-        }
-        float mx_a, mx_b;
-        if (!neg) {
-          mx_a = mx_b = -INFINITY;
+        // Fast path for the common tile (all 64 tokens valid, positive scale); the general
+        // path masks tokens and takes the minimum for a negative scale.
+        const bool general = partial || neg;
+        float mx_a = -INFINITY, mx_b = -INFINITY;
+        if (!general) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             if (i & 2)
@@ -787,26 +772,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
           mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2)) * sc;
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2)) * sc;
         } else {
-          mx_a = mx_b = INFINITY;
+          if (partial) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (i & 2)
-              mx_b = fminf(mx_b, s[i]);
-            else
-              mx_a = fminf(mx_a, s[i]);
+            for (int i = 0; i < 32; ++i) {
+              const int col = 8 * (i >> 2) + 2 * t4 + (i & 1);
+              if (col >= nvalid || ((bm >> (col >> g_log2)) & 1u)) s[i] = neg ? INFINITY : -INFINITY;
+            }
           }
-          mx_a = fminf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-          mx_b = fminf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-          mx_a = fminf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-          mx_b = fminf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+          if (!neg) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i & 2)
+                mx_b = fmaxf(mx_b, s[i]);
+              else
+                mx_a = fmaxf(mx_a, s[i]);
+            }
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+          } else {
+            mx_a = mx_b = INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i & 2)
+                mx_b = fminf(mx_b, s[i]);
+              else
+                mx_a = fminf(mx_a, s[i]);
+            }
+            mx_a = fminf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+            mx_b = fminf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+            mx_a = fminf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+            mx_b = fminf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+          }
+          // A row whose tokens are all masked in this tile has no maximum here (and a zero
+          // scale must not turn the infinite mask value into NaN).
+          mx_a = isinf(mx_a) ? -INFINITY : mx_a * sc;
+          mx_b = isinf(mx_b) ? -INFINITY : mx_b * sc;
         }
-        // A row whose tokens are all masked in this tile has no maximum here (and a zero
-        // scale must not turn the infinite mask value into NaN).
-        mx_a = isinf(mx_a) ? -INFINITY : mx_a * sc;
-        mx_b = isinf(mx_b) ? -INFINITY : mx_b * sc;
         if (kSinBufs == 2 && j > 0 && !take_running_max()) {
           ok = false;
           break;
@@ -834,11 +840,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         m_b = mn_b;
         uint32_t pw[16];
         float sum_a = 0.f, sum_b = 0.f;
+        if (!partial) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float p0 = ex2(fmaf(s[4 * k], sc, -mn_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -mn_a));
-          float p2 = ex2(fmaf(s[4 * k + 2], sc, -mn_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -mn_b));
-          if (partial) {
+          for (int k = 0; k < 8; ++k) {
+            const float p0 = ex2(fmaf(s[4 * k], sc, -mn_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -mn_a));
+            const float p2 = ex2(fmaf(s[4 * k + 2], sc, -mn_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -mn_b));
+            sum_a += p0 + p1;
+            sum_b += p2 + p3;
+            pw[2 * k] = pack2(p0, p1, kFp16);
+            pw[2 * k + 1] = pack2(p2, p3, kFp16);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            float p0 = ex2(fmaf(s[4 * k], sc, -mn_a)), p1 = ex2(fmaf(s[4 * k + 1], sc, -mn_a));
+            float p2 = ex2(fmaf(s[4 * k + 2], sc, -mn_b)), p3 = ex2(fmaf(s[4 * k + 3], sc, -mn_b));
             // Masked tokens weigh exactly 0, also when the row has no maximum yet.
             const int c0 = 8 * k + 2 * t4;
             const bool v0 = c0 < nvalid && !((bm >> (c0 >> g_log2)) & 1u);
@@ -847,11 +863,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             p2 = v0 ? p2 : 0.f;
             p1 = v1 ? p1 : 0.f;
             p3 = v1 ? p3 : 0.f;
+            sum_a += p0 + p1;
+            sum_b += p2 + p3;
+            pw[2 * k] = pack2(p0, p1, kFp16);
+            pw[2 * k + 1] = pack2(p2, p3, kFp16);
           }
-          sum_a += p0 + p1;
-          sum_b += p2 + p3;
-          pw[2 * k] = pack2(p0, p1, kFp16);
-          pw[2 * k + 1] = pack2(p2, p3, kFp16);
         }
         l_a += sum_a;
         l_b += sum_b;
@@ -968,6 +984,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         have_o = waiter.wait(sh.bar(kBarPvDone0 + (last & 1)), (last >> 1) & 1);
         tc_fence_after();
       }
+      // The tiles below reuse the ring, where Q's latent half landed first (a split with no
+      // tokens never waited for it).
+      drain_wait(sh.bar(kBarQFull), 0, args.wait_ns);
       const float l = lstat[2 * (quarter * 32 + lane)];
       stage_rows<T>(smem_gen + kOffStages, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
                     4 * wg, 4, final_out);
@@ -1135,7 +1154,7 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
       p.dtype == TMLA_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int g = p.block_table ? pow2_rows(p.page_size) : kTile;
   const uint64_t pages = p.block_table ? (uint64_t)p.num_pages : (uint64_t)p.batch;
-  CUtensorMap tm_lat, tm_rope, tm_q, tm_out, tm_part;
+  CUtensorMap tm_lat, tm_rope, tm_q, tm_qlat, tm_out, tm_part;
   memset(&tm_out, 0, sizeof(tm_out));
   memset(&tm_part, 0, sizeof(tm_part));
   int rc = encode3d(&tm_lat, dt, p.kv, 576, (uint64_t)p.page_size, pages, (uint64_t)p.kv_stride_tok * 2,
@@ -1146,6 +1165,9 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   if (!rc)
     rc = encode3d(&tm_q, dt, p.q, 576, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.q_stride_h * 2,
                   (uint64_t)p.q_stride_b * 2, kHalfRope, 128, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!rc)
+    rc = encode3d(&tm_qlat, dt, p.q, 576, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.q_stride_h * 2,
+                  (uint64_t)p.q_stride_b * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   // The final 16-bit output (one split) and the fp32 partials (several) as tensor maps;
   // a plan of per-request splits can need both in one launch.
   const bool any_final = units ? num_slots < num_units : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
@@ -1182,12 +1204,12 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   if (p.dtype == TMLA_DTYPE_FP16) {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__half>, tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
+      e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__half>, tm_lat, tm_rope, tm_out, tm_part, tm_q, tm_qlat, a);
   } else {
     e = cudaFuncSetAttribute(mla_sm100_split_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes);
     if (e == cudaSuccess)
-      e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__nv_bfloat16>, tm_lat, tm_rope, tm_out, tm_part, tm_q, a);
+      e = cudaLaunchKernelEx(&cfg, mla_sm100_split_kernel<__nv_bfloat16>, tm_lat, tm_rope, tm_out, tm_part, tm_q, tm_qlat, a);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;
