@@ -197,13 +197,16 @@ def run_layer(args, cfg, device, world, rank, local):
     lens = torch.full((B,), ctx, dtype=torch.int32, device=device)
     x = torch.randn(B, mcfg.hidden_size, generator=g, device=device, dtype=torch.bfloat16)
     splits = get_num_splits(B, 128, ctx + 1, torch.cuda.get_device_properties(device).multi_processor_count)
-    # The library's launches per step: kv append (+ q_norm), q absorb, W_UV, the decode (+ merge),
-    # and the wq_b / wo projections that take the tcgen05 projection kernel.
+    # The library's launches per step: kv append (+ q_norm), the decode query's RoPE and W_UK
+    # product, W_UV, the decode (+ merge), and the projections that take the tcgen05 projection
+    # kernel ([wq_a; wkv_a], wq_b, wo).
     from triton_mla import layer_ops
+    x_rows = torch.empty(B, mcfg.hidden_size, device=device, dtype=torch.bfloat16)
     q_rows = torch.empty(B, mcfg.q_lora_rank, device=device, dtype=torch.bfloat16)
     o_rows = torch.empty(B, mcfg.num_heads * mcfg.v_head_dim, device=device, dtype=torch.bfloat16)
-    layer_launches = 3 + (2 if splits > 1 else 1) + sum(
-        layer_ops.linear_preferred(a, w) for a, w in ((q_rows, layer.wq_b.weight), (o_rows, layer.wo.weight)))
+    layer_launches = 4 + (2 if splits > 1 else 1) + sum(
+        layer_ops.linear_preferred(a, w)
+        for a, w in ((x_rows, layer._w_a()), (q_rows, layer.wq_b.weight), (o_rows, layer.wo.weight)))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     flops, nbytes = layer_counts(B, ctx)
@@ -300,8 +303,8 @@ def run_layer(args, cfg, device, world, rank, local):
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
                      "frac": achieved / peak, "traffic": None, "traffic_source": "not captured for this config",
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
-                     "kernel": "whole layer step (tcgen05 decode and wq_b / wo / W_UV projections, "
-                               "cuBLAS wq_a + wkv_a)",
+                     "kernel": "whole layer step (tcgen05 decode; the [wq_a; wkv_a], wq_b, W_UK, W_UV and "
+                               "wo products on the tcgen05 projection kernel)",
                      "algorithmic_bytes_per_step": nbytes, "algorithmic_flops_per_step": flops},
         "cpu_baseline": cpu,
         "e2e": {"value": world * flops / (float(te.item()) * 1e-3) / 1e12, "unit": "TFLOPS",

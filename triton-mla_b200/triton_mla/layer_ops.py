@@ -121,12 +121,13 @@ def linear_ok(x: torch.Tensor, weight: torch.Tensor) -> bool:
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0)
 
 
-# Below this many weight bytes cuBLAS wins inside the layer step: the projection kernel's
-# fixed costs (a cold start, the ordered sum of split-K partials) outweigh its streaming rate
-# (measured on B200, DeepSeek-V3 layer graph: with [wq_a; wkv_a] (30 MB, 9 split-K pieces per
-# tile) on this kernel the step took 169.1-169.4 us, with it on cuBLAS 168.4 us; wq_b (75 MB)
-# and wo (235 MB) on this kernel beat cuBLAS).
-LINEAR_MIN_WEIGHT_BYTES = 48 << 20
+# From this many weight bytes up a layer step takes the projection kernel (all of the DeepSeek-V3
+# layer's projections: [wq_a; wkv_a] 30 MB, wq_b 75 MB, wo 235 MB); smaller weights go to
+# cuBLAS.  Measured on B200 in the layer graph: wq_b and wo on this kernel beat cuBLAS;
+# [wq_a; wkv_a] (9 split-K pieces per tile, first kernel of the step, nothing to overlap its
+# cold start) costs about 1 us more than cuBLAS there (169.1-169.4 against 168.4 us), which the
+# step pays so that it runs on this library's kernels alone.
+LINEAR_MIN_WEIGHT_BYTES = 16 << 20
 
 
 def linear_preferred(x: torch.Tensor, weight: torch.Tensor) -> bool:
