@@ -46,6 +46,10 @@ extern "C" {
 /* Bits of the device status word (OR-ed by kernels). */
 #define TMLA_STATUS_BAD_PAGE 0x1   /* a block-table entry was outside [0, num_pages); its tokens were masked */
 #define TMLA_STATUS_TIMEOUT 0x2    /* a bounded pipeline wait gave up; the result is invalid */
+#define TMLA_STATUS_RANGE 0x4      /* FP8 rows on the tcgen05 kernel, whose latent products are fp16: a query
+                                      value, a RoPE value or a row scale (times 448, the largest e4m3
+                                      value) was beyond the fp16 range; those rows may hold inf / NaN
+                                      (TMLA_KERNEL_GENERIC computes such rows in fp32) */
 
 /* Element types of q / kv_cache / out. */
 #define TMLA_DTYPE_BF16 0
@@ -55,7 +59,7 @@ extern "C" {
 /* Kernel selection for tmla_decode / tmla_decode_partial. */
 #define TMLA_KERNEL_AUTO 0         /* tcgen05 kernel when the shape allows it, else the generic kernel */
 #define TMLA_KERNEL_GENERIC 1      /* CUDA-core split-KV kernel: any power-of-two head_dim_v / rope dim */
-#define TMLA_KERNEL_SM100 2        /* TMA + tcgen05 + TMEM kernel: d_qk 576, d_v 512, 16-bit types */
+#define TMLA_KERNEL_SM100 2        /* TMA + tcgen05 + TMEM kernel: d_qk 576, d_v 512, 16-bit q, 16-bit or FP8 rows */
 
 /* Flags. */
 #define TMLA_FLAG_PARTIAL_ONLY 0x1  /* write ws_o / ws_lse even when num_splits == 1 (stage-1 semantics) */
@@ -68,9 +72,12 @@ extern "C" {
    TMLA_KV_SAME: d_qk values of the q dtype per token.
    TMLA_KV_FP8_E4M3: 656 bytes per token (d_qk 576, d_v 512): 512 float8 e4m3 latent values,
    4 fp32 scales (scale i multiplies latent values 128 i .. 128 i + 127), then the 64 RoPE
-   values in bf16.  The kv strides count bytes.  q and out are bf16 or fp16; the CUDA-core
-   kernel runs it.  The reference has no FP8 cache; the layout is the public 656-byte FP8 MLA
-   cache row of FlashMLA (DeepSeek-V3.2). */
+   values in bf16.  The kv strides count bytes.  q and out are bf16 or fp16.  The tcgen05
+   kernel (16-byte aligned rows and strides) dequantises each tile in shared memory and forms
+   the latent products in fp16 (value = e4m3 x scale rounded to fp16 once, relative error
+   <= 2^-11; queries converted to fp16), flagging TMLA_STATUS_RANGE for values beyond fp16;
+   the CUDA-core kernel computes in fp32.  The reference has no FP8 cache; the layout is the
+   public 656-byte FP8 MLA cache row of FlashMLA (DeepSeek-V3.2). */
 #define TMLA_KV_SAME 0
 #define TMLA_KV_FP8_E4M3 1
 

@@ -46,7 +46,7 @@ def test_abi_version_and_struct_layout():
     # Header constants match the binding's.
     text = HEADER.read_text()
     for name in ("OK", "ERR_INVALID_ARG", "ERR_UNSUPPORTED", "ERR_MISALIGNED", "ERR_CUDA", "ERR_WORKSPACE",
-                 "STATUS_BAD_PAGE", "STATUS_TIMEOUT", "DTYPE_BF16", "DTYPE_FP16", "DTYPE_FP32", "KERNEL_AUTO",
+                 "STATUS_BAD_PAGE", "STATUS_TIMEOUT", "STATUS_RANGE", "DTYPE_BF16", "DTYPE_FP16", "DTYPE_FP32", "KERNEL_AUTO",
                  "KERNEL_GENERIC", "KERNEL_SM100", "FLAG_PARTIAL_ONLY"):
         m = re.search(rf"#define TMLA_{name}\s+(0x[0-9a-fA-F]+|\d+)", text)
         assert m and int(m.group(1), 0) == getattr(_lib, name), name

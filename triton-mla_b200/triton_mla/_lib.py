@@ -33,6 +33,7 @@ KV_FP8_E4M3 = 1
 
 STATUS_BAD_PAGE = 0x1
 STATUS_TIMEOUT = 0x2
+STATUS_RANGE = 0x4      # FP8 rows on the tcgen05 kernel: a value beyond the fp16 range
 
 DTYPE_BF16 = 0
 DTYPE_FP16 = 1

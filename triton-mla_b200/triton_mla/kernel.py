@@ -197,8 +197,10 @@ def read_status(device=None, reset: bool = True) -> int:
     """Read (and by default clear) the device status word of ``device``.
 
     Bits: ``_lib.STATUS_BAD_PAGE`` (a block-table entry outside the page pool
-    or a length beyond the cache; those tokens were masked) and
-    ``_lib.STATUS_TIMEOUT`` (a bounded pipeline wait gave up).  Synchronises.
+    or a length beyond the cache; those tokens were masked),
+    ``_lib.STATUS_TIMEOUT`` (a bounded pipeline wait gave up) and ``_lib.STATUS_RANGE``
+    (FP8 rows on the tcgen05 kernel: a query, RoPE value or row scale beyond the range of its
+    fp16 products; ``kernel="generic"`` computes such rows in fp32).  Synchronises.
     """
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     t = _status_word(device)
