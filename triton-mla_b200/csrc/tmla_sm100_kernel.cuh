@@ -274,18 +274,41 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool fp16) {
 }
 
 // FP8 rows: sixteen e4m3 values (one 16-byte word, value i in byte i) times `scale` as
-// sixteen fp16 values in two 16-byte words (values 0-7, 8-15).  e4m3 -> fp16 is exact; the
-// product is formed in fp32 and rounded to fp16 once.
+// sixteen fp16 values in two 16-byte words (values 0-7, 8-15), each rounded once.
+// e4m3 -> fp16 is exact (one conversion per pair).  For scales in [2^-10, 146] the product
+// stays in fp16 arithmetic: scale = s_hi + s_lo with s_hi = fp16(scale) and
+// s_lo = fp16(scale - s_hi), and value = fma(x, s_hi, x * s_lo).  x * s_hi is exact inside
+// the fma (4 + 11 significant bits) and x * s_lo is 2^-11 of the value or less, so the one
+// rounding of the fma gives the fp16 nearest to x * scale unless the product lies within
+// about 2^-22 of a rounding midpoint (1.3% of values over all e4m3 values and 4,000 scales,
+// each then one unit in the last place away).
+// Other scales (tiny, or past the fp16 range) take fp32 products.  This keeps the
+// conversions, which run at a fraction of the arithmetic rate, at 11 per 16 values
+// instead of 32.
 __device__ __forceinline__ void dequant16(uint4 v, float scale, uint4& lo, uint4& hi) {
   const uint32_t in[4] = {v.x, v.y, v.z, v.w};
   uint32_t out[8];
+  if (scale >= 0.0009765625f && scale <= 146.f) {
+    const __half2 s_hi = __float2half2_rn(scale);
+    const __half2 s_lo = __float2half2_rn(scale - __low2float(s_hi));
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 4; ++i) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const __half2 x = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> (16 * h)), __NV_E4M3));
-      const float2 f = __half22float2(x);
-      out[2 * i + h] = pack2(f.x * scale, f.y * scale, true);
+      for (int h = 0; h < 2; ++h) {
+        const __half2 x = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> (16 * h)), __NV_E4M3));
+        const __half2 r = __hfma2(x, s_hi, __hmul2_rn(x, s_lo));
+        out[2 * i + h] = *reinterpret_cast<const uint32_t*>(&r);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const __half2 x = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> (16 * h)), __NV_E4M3));
+        const float2 f = __half22float2(x);
+        out[2 * i + h] = pack2(f.x * scale, f.y * scale, true);
+      }
     }
   }
   lo = make_uint4(out[0], out[1], out[2], out[3]);
