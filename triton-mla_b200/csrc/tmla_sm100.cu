@@ -117,11 +117,11 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   memset(&tm_part, 0, sizeof(tm_part));
   int rc;
   if (fp8) {
-    // FP8 rows (656 bytes): the e4m3 latent half of a CTA as 256-byte unswizzled rows, the
-    // scale quadruple (bytes 512-527), and the RoPE half as bf16 elements 264-327.
+    // FP8 rows (656 bytes): the e4m3 latent values as 128-byte swizzled boxes (two per CTA half),
+    // the scale quadruple (bytes 512-527), and the RoPE half as bf16 elements 264-327.
     const uint64_t st = (uint64_t)p.kv_stride_tok, sp = (uint64_t)p.kv_stride_page;
     rc = encode3d(&tm_lat, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.kv, sm100_fp8::kFp8Row, (uint64_t)p.page_size, pages, st,
-                  sp, sm100_fp8::kHalfLatent, (uint32_t)g, CU_TENSOR_MAP_SWIZZLE_NONE);
+                  sp, 128, (uint32_t)g, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc)
       rc = encode3d(&tm_scale, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.kv, sm100_fp8::kFp8Row, (uint64_t)p.page_size, pages,
                     st, sp, 16, (uint32_t)g, CU_TENSOR_MAP_SWIZZLE_NONE);

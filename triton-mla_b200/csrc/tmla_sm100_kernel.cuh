@@ -134,9 +134,11 @@ constexpr uint32_t kPPeerBytes = 64 * kTile * 2;            // 8192: the rows of
 constexpr uint32_t kAlphaBytes = 64 * 4;                    // rescale factors that come with P
 constexpr uint32_t kFinBytes = 64 * 8;                      // final (l, m) of the peer's heads
 constexpr uint32_t kStatBytes = 128 * 8;  // final (l, m) of all 128 rows for the epilogue
-// An FP8 landing slot: 64 tokens x this CTA's 256 e4m3 latent values (256 bytes per token,
-// unswizzled), then the tokens' 16-byte scale quadruples.
+// An FP8 landing slot: this CTA's 256 e4m3 latent values of 64 tokens as two 128B-swizzled
+// boxes of 128 values (8 KB each; token r, 16-byte chunk c at r * 128 + (c ^ (r & 7)) * 16),
+// then the tokens' 16-byte scale quadruples.
 constexpr uint32_t kLandLatBytes = kTile * kHalfLatent;
+constexpr uint32_t kLandBoxBytes = kTile * 128;
 constexpr uint32_t kLandBytes = kLandLatBytes + kTile * 16;
 constexpr uint32_t kFp8Row = 656;         // bytes per token of an FP8 row
 constexpr int kFp8RopeElem = 264;         // its RoPE half starts at byte 528: bf16 element 264
@@ -274,41 +276,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool fp16) {
 }
 
 // FP8 rows: sixteen e4m3 values (one 16-byte word, value i in byte i) times `scale` as
-// sixteen fp16 values in two 16-byte words (values 0-7, 8-15), each rounded once.
-// e4m3 -> fp16 is exact (one conversion per pair).  For scales in [2^-10, 146] the product
-// stays in fp16 arithmetic: scale = s_hi + s_lo with s_hi = fp16(scale) and
-// s_lo = fp16(scale - s_hi), and value = fma(x, s_hi, x * s_lo).  x * s_hi is exact inside
-// the fma (4 + 11 significant bits) and x * s_lo is 2^-11 of the value or less, so the one
-// rounding of the fma gives the fp16 nearest to x * scale unless the product lies within
-// about 2^-22 of a rounding midpoint (1.3% of values over all e4m3 values and 4,000 scales,
-// each then one unit in the last place away).
-// Other scales (tiny, or past the fp16 range) take fp32 products.  This keeps the
-// conversions, which run at a fraction of the arithmetic rate, at 11 per 16 values
-// instead of 32.
+// sixteen fp16 values in two 16-byte words (values 0-7, 8-15).  e4m3 -> fp16 is exact (one
+// conversion per pair); the product is formed in fp32 and rounded to fp16 once.  (Forming it
+// with fp16 FMAs and a scale split into two fp16 parts needs a third of the conversions but
+// measured 6% slower on the whole kernel.)
 __device__ __forceinline__ void dequant16(uint4 v, float scale, uint4& lo, uint4& hi) {
   const uint32_t in[4] = {v.x, v.y, v.z, v.w};
   uint32_t out[8];
-  if (scale >= 0.0009765625f && scale <= 146.f) {
-    const __half2 s_hi = __float2half2_rn(scale);
-    const __half2 s_lo = __float2half2_rn(scale - __low2float(s_hi));
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 4; ++i) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const __half2 x = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> (16 * h)), __NV_E4M3));
-        const __half2 r = __hfma2(x, s_hi, __hmul2_rn(x, s_lo));
-        out[2 * i + h] = *reinterpret_cast<const uint32_t*>(&r);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const __half2 x = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> (16 * h)), __NV_E4M3));
-        const float2 f = __half22float2(x);
-        out[2 * i + h] = pack2(f.x * scale, f.y * scale, true);
-      }
+    for (int h = 0; h < 2; ++h) {
+      const __half2 x = __half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> (16 * h)), __NV_E4M3));
+      const float2 f = __half22float2(x);
+      out[2 * i + h] = pack2(f.x * scale, f.y * scale, true);
     }
   }
   lo = make_uint4(out[0], out[1], out[2], out[3]);
@@ -601,7 +582,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (live && !bad) {
         const int slot = p.block_table ? t % p.page_size : t;
         const uint32_t dst = sh.land(ls), bar = sh.bar(kBarLandFull0 + ls);
-        tma_load_3d(dst + lane * g * kHalfLatent, &tm_kv_lat, bar, kHalfLatent * rank, slot, pg, pol_stream);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb)
+          tma_load_3d(dst + hb * kLandBoxBytes + lane * g * 128, &tm_kv_lat, bar, kHalfLatent * rank + 128 * hb, slot,
+                      pg, pol_stream);
         tma_load_3d(dst + kLandLatBytes + lane * g * 16, &tm_kv_scale, bar, 512, slot, pg, pol_stream);
         tma_load_3d(sh.rope(rs) + lane * g * (kHalfRope * 2), &tm_kv_rope, bar, kFp8RopeElem + kHalfRope * rank, slot,
                     pg, pol_stream);
@@ -795,16 +779,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (kFp8 && warp >= 16) {
     // ------------------------------------------------------------ FP8 rows: dequantising warpgroup
-    // Thread t takes the 16-value chunk k = t % 16 of this CTA's 256 latent values (scale
-    // group 2 rank + k / 8) for tokens t / 16 + 8u, u = 0..7: a warp reads 512 contiguous
-    // bytes of the landing slot and writes fp16 into the 128B-swizzled boxes QK and PV read
-    // (token r, 16-byte column c of a box at r * 128 + (c ^ (r & 7)) * 16).  Masked tokens
-    // (past the split or in a sub-box that was not loaded) are written as zeros.
+    // Thread t takes the 16-value chunk k = t / 8 of this CTA's 256 latent values (scale group
+    // 2 rank + k / 8) for tokens r = t % 8 + 8u, u = 0..7.  The eight threads of each quarter-warp
+    // phase of a 16-byte access hold eight tokens with r & 7 = 0..7, so their reads of the
+    // swizzled landing boxes and their writes into the 128B-swizzled ring boxes QK and PV read
+    // (token r, 16-byte chunk c at r * 128 + (c ^ (r & 7)) * 16) fall in eight different bank
+    // groups.  Masked tokens (past the split or in a sub-box that was not loaded) are written
+    // as zeros.
     const int t = threadIdx.x - 512;
-    const int k = t & 15, tok0 = t >> 4;
+    const int rl = t & 7, k = t >> 3;
     const int grp = 2 * (int)rank + (k >> 3);
-    const uint32_t box_off = (uint32_t)(k >> 2) * kBoxBytes;
+    const uint32_t src_off = (uint32_t)(k >> 3) * kLandBoxBytes + (uint32_t)rl * 128u + (uint32_t)(((k & 7) ^ rl) << 4);
     const int c0 = 2 * (k & 3);
+    const uint32_t dst_off0 = (uint32_t)(k >> 2) * kBoxBytes + (uint32_t)rl * 128u + (uint32_t)((c0 ^ rl) << 4);
+    const uint32_t dst_off1 = (uint32_t)(k >> 2) * kBoxBytes + (uint32_t)rl * 128u + (uint32_t)(((c0 + 1) ^ rl) << 4);
     bool range = false, ok = true;
     // Every lane waits (each reads what the barrier guards); a warp leaves together.
     auto wait_warp = [&](uint32_t bar, uint32_t parity) {
@@ -835,20 +823,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t bm = land_mask[ls];
       const int nvalid = min(kTile, end - (start + j * kTile));
       const unsigned char* src = smem_gen + kOffLand + ls * kLandBytes;
-      unsigned char* dst = smem_gen + kOffStages + s * kStageBytes + box_off;
+      unsigned char* dst = smem_gen + kOffStages + s * kStageBytes;
 #pragma unroll 2
       for (int u = 0; u < 8; ++u) {
-        const int r = tok0 + 8 * u;
+        const int r = rl + 8 * u;
         uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
         if (r < nvalid && !((bm >> (r >> g_log2)) & 1u)) {
-          const uint4 v = *reinterpret_cast<const uint4*>(src + r * kHalfLatent + k * 16);
+          const uint4 v = *reinterpret_cast<const uint4*>(src + src_off + u * 1024);
           const float sc = *reinterpret_cast<const float*>(src + kLandLatBytes + r * 16 + grp * 4);
           // A scale that can take an e4m3 value (at most 448) past the fp16 range.
           range |= !(fabsf(sc) * 448.f < 65520.f);
           dequant16(v, sc, lo, hi);
         }
-        *reinterpret_cast<uint4*>(dst + r * 128 + ((c0 ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4*>(dst + r * 128 + (((c0 + 1) ^ (r & 7)) << 4)) = hi;
+        *reinterpret_cast<uint4*>(dst + dst_off0 + u * 1024) = lo;
+        *reinterpret_cast<uint4*>(dst + dst_off1 + u * 1024) = hi;
       }
       if (kFp16) {
         // fp16 queries: the tile's bf16 RoPE values -> fp16 in place (the RoPE QK steps are fp16).
