@@ -803,6 +803,56 @@ def test_fp8_cache_beyond_fp16_range_is_flagged(device, monkeypatch):
     assert rel <= 1e-2
 
 
+def test_fp8_cache_ragged_batch_with_a_split_plan(device):
+    """FP8 rows through the per-request split plan (num_splits=None in eager mode), with a long
+    request cut into several splits merged from partial slots."""
+    from triton_mla import fp8_cache
+    from triton_mla.kernel import plan_units
+    lens = [65536, 1, 300, 0, 4097, 64, 12000]
+    units, _ = plan_units(lens, 128)
+    assert units[units[:, 0] == 0][0, 2] > 1, "the long request is split"
+    case = recipes.paged_case(lens, 128, 64, seed=93)
+    rows = fp8_cache.quantize_kv(case["kv"])
+    ref_out, ref_lse = oracle_of(dict(case, kv=fp8_cache.dequantize_kv(rows)))
+    c = to_dev(dict(case, kv=rows), device)
+    out, lse = mla_decode(c["q"], c["kv"], c["seqlens"], c["block_table"], softmax_scale=c["scale"],
+                          return_lse=True)
+    check(out, lse, ref_out, ref_lse, lens, lse_tol=FP8_LSE_TOL["auto"])
+    assert read_status(device) == 0
+
+
+def test_fp8_cache_device_plan_in_a_graph(device):
+    """FP8 rows with the device planner, the split kernel and the merge captured in one CUDA
+    graph and replayed as the lengths change."""
+    from triton_mla import fp8_cache, make_device_split_plan
+    lens0 = [4096, 100, 0, 7000, 33, 20000]
+    case = recipes.paged_case(lens0, 128, 64, seed=94)
+    rows = fp8_cache.quantize_kv(case["kv"])
+    deq = fp8_cache.dequantize_kv(rows)
+    c = to_dev(dict(case, kv=rows), device)
+    lens = c["seqlens"].clone()
+    plan = make_device_split_plan(lens, 128)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        plan.refresh(lens)
+        mla_decode(c["q"], c["kv"], lens, c["block_table"], softmax_scale=c["scale"], return_lse=True, plan=plan)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        plan.refresh(lens)
+        g_out, g_lse = mla_decode(c["q"], c["kv"], lens, c["block_table"], softmax_scale=c["scale"],
+                                  return_lse=True, plan=plan)
+    for new in (lens0, [20000, 1, 1, 1, 1, 1], [5000, 5000, 5000, 5000, 5000, 5000]):
+        lens.copy_(torch.tensor(new, dtype=torch.int32, device=device))
+        graph.replay()
+        torch.cuda.synchronize(device)
+        ref_out, ref_lse = oracle_of(dict(case, kv=deq, seqlens=torch.tensor(new, dtype=torch.int32)))
+        check(g_out, g_lse, ref_out, ref_lse, new, lse_tol=FP8_LSE_TOL["auto"])
+        assert read_status(device) == 0
+    del graph
+
+
 def test_fp8_cache_full_config_against_oracle(device):
     """BASELINE config 2 with FP8 rows (B=32, S=4096, page 64) on the tcgen05 kernel: every
     request against the oracle over its dequantised rows."""
