@@ -29,7 +29,7 @@
 //     duplicated.  Both CTAs' PV commits are counted on a barrier in each CTA,
 //     so a P buffer is rewritten only after both CTAs have read it.
 // Cache tiles flow through two rings: the latent part (V as well as K) is held
-// until PV (4 stages), the RoPE part only until QK (2 slots).  Score and P
+// until PV (4 stages), the RoPE part only until QK (4 slots).  Score and P
 // buffers are double-buffered and QK and PV are issued by different warps, so
 // QK of tile j+1 and the score swap of tile j+1 run while tile j is in the
 // softmax.
@@ -112,7 +112,7 @@ using namespace ptx;
 constexpr bool kFp8 = TMLA_SM100_FP8 != 0;
 constexpr int kTile = 64;                 // tokens per pipeline stage
 constexpr int kStages = 4;                // latent cache-tile ring depth (held until PV)
-constexpr int kRopeSlots = kFp8 ? 3 : 2;  // RoPE cache-tile ring depth (held until QK)
+constexpr int kRopeSlots = kFp8 ? 3 : 4;  // RoPE cache-tile ring depth (held until QK)
 constexpr int kLandSlots = 2;             // FP8 landing slots (FP8 rows only)
 constexpr int kSinBufs = kFp8 ? 1 : 2;    // score-exchange buffers (1 or 2)
 constexpr int kPBufs = kFp8 ? 1 : 2;      // P buffers, the A operand of PV (1 or 2)
