@@ -792,8 +792,12 @@ def main(argv=None):
     q_d = [torch.empty_like(q) for _ in range(nbuf)]
     lens_d = [torch.empty_like(lens) for _ in range(nbuf)]
     bt_d = [torch.empty_like(bt) for _ in range(nbuf)]
+    # The output of each buffer set is allocated once and passed as mla_decode's `out=` (the
+    # host's work per step is then the copies, the flush and one mla_decode call).
+    o_d = [torch.empty(o_shape, dtype=q.dtype, device=device) for _ in range(nbuf)]
     in_ready = [torch.cuda.Event() for _ in range(nbuf)]
     decoded = [torch.cuda.Event() for _ in range(nbuf)]
+    downloaded = [torch.cuda.Event() for _ in range(nbuf)]
 
     def e2e_steps(n):
         for i in range(n):
@@ -806,15 +810,17 @@ def main(argv=None):
                 bt_d[k].copy_(bt_h, non_blocking=True)
                 in_ready[k].record(s_in)
             stream.wait_event(in_ready[k])
+            if i >= nbuf:
+                stream.wait_event(downloaded[k])  # step i - nbuf's output has left buffer set k
             flush.zero_()
             o, l = mla_decode(q_d[k], kv, lens_d[k], bt_d[k], softmax_scale=SCALE, num_splits=splits,
-                              return_lse=True, kernel=args.kernel, plan=plan)
+                              return_lse=True, kernel=args.kernel, plan=plan, out=o_d[k])
             decoded[k].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(decoded[k])
                 out_h[k].copy_(o, non_blocking=True)
                 lse_h[k].copy_(l, non_blocking=True)
-            o.record_stream(s_out)
+                downloaded[k].record(s_out)
             l.record_stream(s_out)
 
     e2e_steps(args.warmup)

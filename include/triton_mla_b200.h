@@ -299,6 +299,15 @@ typedef struct TmlaOUnabsorbParams {
 } TmlaOUnabsorbParams;
 int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream);
 
+/* L2 prefetch (no counterpart in the reference): brings count chunks of chunk_bytes at
+   base + i * stride_bytes into L2, as bulk prefetches issued by ctas one-warp CTAs, and returns
+   without waiting for them.  The layer step runs it on a side stream during the decode, which
+   leaves HBM bandwidth and SMs idle, for the weights the products after the decode read (W_UV
+   and the first part of wo).  base, chunk_bytes and stride_bytes must be multiples of 16
+   (else TMLA_ERR_MISALIGNED); it reads nothing into the caller's memory and writes nothing. */
+int tmla_l2_prefetch(const void* base, int64_t chunk_bytes, int64_t stride_bytes, int32_t count, int32_t ctas,
+                     void* stream);
+
 /* y[i, j] = sum_c x[i, c] w[j, c] for m <= 64 rows of x: a bias-free nn.Linear of a decode
    batch (replaces the cuBLAS GEMMs behind the reference layer's wq_a, wkv_a, wq_b and wo,
    model.py:104-108,124), streaming w once through tcgen05 MMAs on every SM.  With groups > 1

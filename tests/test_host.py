@@ -339,3 +339,30 @@ def test_decode_is_a_registered_torch_operator_with_a_meta_kernel():
     out = torch.empty(4, 128, 512, dtype=torch.bfloat16, device=meta)
     lse = torch.empty(4, 128, dtype=torch.float32, device=meta)
     op(q, kv, lens, bt, out, lse, 2, 0.07, 0, 1, None)
+
+
+@pytest.mark.parametrize("args, code", [
+    ((256, 32, 32, 1, 1), _lib.OK),                    # count 0 below: nothing to do, nothing launched
+    ((0, 32, 32, 1, 1), _lib.ERR_INVALID_ARG),         # null base
+    ((256, 0, 32, 1, 1), _lib.ERR_INVALID_ARG),        # empty chunk
+    ((256, 32, 16, 1, 1), _lib.ERR_INVALID_ARG),       # chunks overlap (stride < chunk)
+    ((256, 32, 32, 1, 0), _lib.ERR_INVALID_ARG),       # no CTAs
+    ((256, 32, 32, -1, 1), _lib.ERR_INVALID_ARG),      # negative count
+    ((264, 32, 32, 1, 1), _lib.ERR_MISALIGNED),        # base not 16-byte aligned
+    ((256, 24, 32, 1, 1), _lib.ERR_MISALIGNED),        # chunk not a multiple of 16
+    ((256, 32, 40, 1, 1), _lib.ERR_MISALIGNED),        # stride not a multiple of 16
+])
+def test_l2_prefetch_rejects_bad_arguments_before_any_launch(args, code):
+    """tmla_l2_prefetch checks its arguments before it launches anything (the first case has
+    count 0, which returns at once)."""
+    base, chunk, stride, count, ctas = args
+    if code == _lib.OK:
+        count = 0
+    rc = _lib.load().tmla_l2_prefetch(ctypes.c_void_p(base), chunk, stride, count, ctas, None)
+    assert rc == code
+
+
+def test_l2_prefetch_helper_refuses_cpu_tensors():
+    from triton_mla import layer_ops
+    with pytest.raises(AssertionError):
+        layer_ops.l2_prefetch(torch.zeros(64, dtype=torch.bfloat16))

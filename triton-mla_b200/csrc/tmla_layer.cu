@@ -590,6 +590,21 @@ __global__ void __launch_bounds__(128) o_unabsorb_mma_kernel(TmlaOUnabsorbParams
   }
 }
 
+// L2 prefetch of `count` chunks of `chunk` bytes at base + i * stride (no shared memory, no
+// completion: a hint that the next kernels' operands should be in L2).  Each lane issues bulk
+// prefetches of at most kPrefetchPiece bytes, pieces dealt round-robin over the grid's lanes.
+constexpr int64_t kPrefetchPiece = 32 << 10;
+__global__ void __launch_bounds__(32) l2_prefetch_kernel(const char* base, int64_t chunk, int64_t stride, int32_t count) {
+  const int64_t per_chunk = (chunk + kPrefetchPiece - 1) / kPrefetchPiece;
+  const int64_t pieces = per_chunk * count;
+  for (int64_t i = (int64_t)blockIdx.x * 32 + threadIdx.x; i < pieces; i += (int64_t)gridDim.x * 32) {
+    const int64_t c = i / per_chunk, off = (i - c * per_chunk) * kPrefetchPiece;
+    const int64_t bytes = chunk - off < kPrefetchPiece ? chunk - off : kPrefetchPiece;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + c * stride + off), "r"((uint32_t)bytes)
+                 : "memory");
+  }
+}
+
 }  // namespace layer
 }  // namespace tmla
 
@@ -797,6 +812,16 @@ int tmla_o_unabsorb(const TmlaOUnabsorbParams* p, void* stream) {
       if (e == cudaSuccess) e = launch(pdl, o_unabsorb_kernel<float>, grid, block, smem, s, *p);
   }
   if (e != cudaSuccess) return tmla::record_cuda_error(e);
+  return finish_launch();
+}
+
+int tmla_l2_prefetch(const void* base, int64_t chunk_bytes, int64_t stride_bytes, int32_t count, int32_t ctas,
+                     void* stream) {
+  if (count == 0) return TMLA_OK;
+  if (!base || chunk_bytes <= 0 || count < 0 || ctas < 1 || stride_bytes < chunk_bytes) return TMLA_ERR_INVALID_ARG;
+  if ((uintptr_t)base % 16 || chunk_bytes % 16 || stride_bytes % 16) return TMLA_ERR_MISALIGNED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  l2_prefetch_kernel<<<ctas, 32, 0, s>>>(static_cast<const char*>(base), chunk_bytes, stride_bytes, count);
   return finish_launch();
 }
 

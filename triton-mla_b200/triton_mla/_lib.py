@@ -64,6 +64,7 @@ EXPORTED = (
     "tmla_q_absorb_rope",
     "tmla_kv_norm_rope_append",
     "tmla_o_unabsorb",
+    "tmla_l2_prefetch",
     "tmla_plan_units",
     "tmla_units_workspace_bytes",
     "tmla_decode_units",
@@ -283,6 +284,8 @@ def load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(st), vp]
         fn.restype = ctypes.c_int
+    lib.tmla_l2_prefetch.argtypes = [vp, i64, i64, i32, i32, vp]
+    lib.tmla_l2_prefetch.restype = ctypes.c_int
     if lib.tmla_abi_version() != ABI_VERSION:
         raise ImportError(f"{path}: ABI version {lib.tmla_abi_version()} != {ABI_VERSION}; rebuild it")
     if lib.tmla_params_bytes() != ctypes.sizeof(TmlaDecodeParams):

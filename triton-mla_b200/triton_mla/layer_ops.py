@@ -1,6 +1,7 @@
 """The MLA layer's per-step operations around the decode kernel, one CUDA launch each
 (C ABI: ``tmla_q_absorb_rope``, ``tmla_kv_norm_rope_append``, ``tmla_o_unabsorb``,
-``tmla_linear``).
+``tmla_linear``), and an L2 prefetch of the weights the step reads after its decode
+(``tmla_l2_prefetch``).
 
 They replace the PyTorch glue of the reference's ``MLA.forward``
 (src/triton_mla/model.py:74-94 and 111-123): RoPE of q_pe and k_pe, kv_norm, the
@@ -200,3 +201,16 @@ def linear(x: torch.Tensor, weight: torch.Tensor, overlap: bool = False,
     _linear_launch(x, x.stride(0), 0, weight, weight.stride(0), 0, _lib.W_NK, y, n, 0, m, n, k, 1, overlap,
                    workspace)
     return y
+
+
+def l2_prefetch(t: torch.Tensor, chunk_bytes: int = None, stride_bytes: int = None, count: int = 1,
+                ctas: int = 16) -> None:
+    """Bring ``count`` chunks of ``chunk_bytes`` starting at ``t``'s data, ``stride_bytes``
+    apart, into L2 (bulk prefetches on the current stream; nothing waits for them).  Defaults:
+    one chunk of the whole tensor.  A hint with no effect on any result."""
+    nbytes = t.numel() * t.element_size()
+    chunk = nbytes if chunk_bytes is None else int(chunk_bytes)
+    stride = chunk if stride_bytes is None else int(stride_bytes)
+    assert t.is_cuda and 0 < chunk and stride >= chunk and (count - 1) * stride + chunk <= nbytes
+    _lib.check(_lib.load().tmla_l2_prefetch(ctypes.c_void_p(t.data_ptr()), chunk, stride, int(count), int(ctas),
+                                             _stream(t)), "tmla_l2_prefetch")

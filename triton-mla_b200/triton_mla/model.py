@@ -143,6 +143,39 @@ class MLA(nn.Module):
             ws = self.__dict__["_linear_workspace"] = layer_ops.LinearWorkspace()
         return ws
 
+    # Bytes of wo brought into L2 during the decode (with all of W_UV); negative: no prefetch.
+    # Config 5 (B200): none 174.5-175.6 µs per step, W_UV only 173.9, + 32 MB of wo 170.3,
+    # + 64 MB 170.9-172.7, + 96 MB 174.2 (more is evicted by the decode's cache stream).
+    l2_prefetch_wo_bytes = 32 << 20
+
+    def _side_stream(self, device):
+        """A stream of this layer for work beside the decode (made once per device)."""
+        streams = self.__dict__.setdefault("_side_streams", {})
+        if device not in streams:
+            streams[device] = torch.cuda.Stream(device)
+        return streams[device]
+
+    def _prefetch_after_decode(self, device):
+        """On a side stream that starts with the decode: W_UV (the rows of wkv_b that o_unabsorb
+        reads) and the first ``l2_prefetch_wo_bytes`` of wo into L2.  The decode is latency-bound
+        and leaves HBM bandwidth and 20 SMs idle; the two products after it stream these weights.
+        Returns the side stream (joined by the caller), or None."""
+        if self.l2_prefetch_wo_bytes < 0:
+            return None
+        cfg = self.cfg
+        side = self._side_stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        w = self.wkv_b.weight
+        row = w.shape[1] * w.element_size()
+        wo = self.wo.weight
+        with torch.cuda.stream(side):
+            layer_ops.l2_prefetch(w[cfg.qk_nope_head_dim:], cfg.v_head_dim * row,
+                                  (cfg.qk_nope_head_dim + cfg.v_head_dim) * row, cfg.num_heads)
+            nbytes = min(self.l2_prefetch_wo_bytes, wo.numel() * wo.element_size()) // 16 * 16
+            if nbytes > 0:
+                layer_ops.l2_prefetch(wo, nbytes)
+        return side
+
     def _proj(self, inp, weight, overlap):
         """``F.linear(inp, weight)``: the weight-streaming tcgen05 kernel for up to 64 tokens and
         a large weight (``layer_ops.linear_preferred``), else cuBLAS.  ``overlap`` as in
@@ -168,10 +201,14 @@ class MLA(nn.Module):
         q = self._proj(qn, self.wq_b.weight, True).view(batch, cfg.num_heads, cfg.qk_head_dim)
         q_full = layer_ops.q_absorb_rope(q, self.wkv_b.weight, positions, cfg.qk_nope_head_dim, cfg.v_head_dim,
                                          cfg.rope_theta, overlap=True)
+        side = self._prefetch_after_decode(x.device)
         o = mla_decode(q_full, kv_cache, seqlens, bt, head_dim_v=cfg.kv_lora_rank, softmax_scale=self.softmax_scale,
                        num_splits=num_splits)
         o = layer_ops.o_unabsorb(o, self.wkv_b.weight, cfg.qk_nope_head_dim, cfg.v_head_dim, overlap=True)
-        return self._proj(o, self.wo.weight, True), seqlens.to(cache_seqlens.dtype)
+        y = self._proj(o, self.wo.weight, True)
+        if side is not None:
+            torch.cuda.current_stream(x.device).wait_stream(side)
+        return y, seqlens.to(cache_seqlens.dtype)
 
     def _forward_ops(self, x, kv_cache, cache_seqlens, block_table, num_splits):
         """The decode step as PyTorch ops around ``mla_decode`` (mixed dtypes)."""
