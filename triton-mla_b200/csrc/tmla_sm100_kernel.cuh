@@ -111,11 +111,11 @@ using namespace ptx;
 // pays for the landing slots with single score-exchange and P buffers.
 constexpr bool kFp8 = TMLA_SM100_FP8 != 0;
 constexpr int kTile = 64;                 // tokens per pipeline stage
-constexpr int kStages = 4;                // latent cache-tile ring depth (held until PV)
+constexpr int kStages = kFp8 ? 3 : 4;     // latent cache-tile ring depth (held until PV)
 constexpr int kRopeSlots = kFp8 ? 3 : 4;  // RoPE cache-tile ring depth (held until QK)
 constexpr int kLandSlots = 2;             // FP8 landing slots (FP8 rows only)
-constexpr int kSinBufs = kFp8 ? 1 : 2;    // score-exchange buffers (1 or 2)
-constexpr int kPBufs = kFp8 ? 1 : 2;      // P buffers, the A operand of PV (1 or 2)
+constexpr int kSinBufs = 2;              // score-exchange buffers (1 or 2)
+constexpr int kPBufs = 2;                // P buffers, the A operand of PV (1 or 2)
 static_assert(kSinBufs == 1 || kSinBufs == 2, "score-exchange buffers");
 static_assert(kPBufs == 1 || kPBufs == 2, "P buffers");
 constexpr int kThreads = kFp8 ? 640 : 512;  // FP8: + warps 16-19, the dequantising warpgroup
@@ -128,6 +128,7 @@ constexpr uint32_t kRowBytes = (kHalfLatent + kHalfRope) * 2;  // cache bytes pe
 constexpr uint32_t kQBoxBytes = 128 * 128;                  // 128 heads x 64 dims, swizzled
 constexpr uint32_t kQRopeBytes = 128 * kHalfRope * 2;       // 8192
 constexpr uint32_t kQLatBytes = 4 * kQBoxBytes;             // this CTA's 256 latent dims of 128 heads
+constexpr int kQStage = kStages - 2;  // Q's latent half lands in the last two ring stages
 constexpr uint32_t kSinBytes = 64 * kTile * 4;              // 16384: peer's partial S for my 64 heads
 constexpr uint32_t kPBufBytes = 128 * kTile * 2;            // 16384: P of all 128 rows, SW128 K-major
 constexpr uint32_t kPPeerBytes = 64 * kTile * 2;            // 8192: the rows of P that come from the peer
@@ -158,8 +159,11 @@ constexpr uint32_t kOffBar = kOffWst + 2 * 64 * 8;
 constexpr uint32_t kOffFin = kOffRope;
 constexpr uint32_t kOffStat = kOffRope + kFinBytes;
 static_assert(kFinBytes + kStatBytes <= kRopeSlots * kRopeBytes, "epilogue scratch must fit in the RoPE ring");
-static_assert(kOffPBuf % 1024 == 0, "P buffers must be 1024-byte aligned for the 128-byte swizzle");
-static_assert(kStages * kStageBytes >= 8 * 128 * 128, "the epilogue tiles (128 KB) reuse the cache-tile ring");
+static_assert(kOffPBuf % 1024 == 0 && kOffSin % 1024 == 0,
+              "P buffers and epilogue tiles must be 1024-byte aligned for the 128-byte swizzle");
+// Epilogue tiles (8 of 16 KB for fp32 partials, 4 for the final output) reuse the cache-tile
+// ring and, past its end, the score-exchange buffers.
+static_assert(kStages * kStageBytes + kSinBufs * kSinBytes >= 8 * 128 * 128, "no room for the epilogue tiles");
 constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 40;
 constexpr uint32_t kOffMisc = kOffBar + ((kNumBars * 8 + 63) / 64) * 64;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
@@ -212,8 +216,8 @@ enum : uint32_t {
   kBarMaxB0 = kBarMaxA0 + 4,  // warpgroup B (odd tiles), per quarter
   kBarWgStats = kBarMaxB0 + 4,  // both warpgroups' final (l, m) are in shared memory
   kBarEpi,         // the epilogue tiles are staged (8 warps)
-  kBarQCopied,     // Q's latent half has been copied from ring stages 2-3 into TMEM
-  kBarQConv,       // FP8 rows: Q's latent half is fp16 in ring stages 2-3 (4 dequantising warps)
+  kBarQCopied,     // Q's latent half has been copied from its two ring stages into TMEM
+  kBarQConv,       // FP8 rows: Q's latent half is fp16 in its ring stages (4 dequantising warps)
   kBarLandFull0,   // FP8 rows: the loads of landing slot 0 / 1 have landed
   kBarLandEmpty0 = kBarLandFull0 + kLandSlots,  // FP8 rows: landing slot 0 / 1 was dequantised (4 warps)
   kBarCount = kBarLandEmpty0 + kLandSlots,
@@ -356,9 +360,15 @@ __device__ __forceinline__ void zero_masked_rows(unsigned char* stage, int nvali
 // 64 16-bit columns of the final output.  They reuse the cache-tile ring, which is idle
 // once the last PV has completed.
 constexpr uint32_t kOutBoxBytes = 128 * 128;
+// Shared-memory offset of epilogue tile c: the cache-tile ring (idle once the last PV has
+// completed), then the score-exchange buffers (read for the last time before the last P).
+__host__ __device__ constexpr uint32_t out_box_off(int c) {
+  return c < 2 * kStages ? kOffStages + (uint32_t)c * kOutBoxBytes
+                         : kOffSin + (uint32_t)(c - 2 * kStages) * kOutBoxBytes;
+}
 
 // Stage columns [32 c0, 32 (c0 + nchunks)) of this CTA's output half of row r (scaled by
-// inv; zeros when there is no output) into the epilogue tiles at `tiles`.
+// inv; zeros when there is no output) into the epilogue tiles (`tiles`: the layout's base).
 template <typename T>
 __device__ __forceinline__ void stage_rows(unsigned char* tiles, uint32_t t_row, bool have_o, int r, float inv,
                                            int c0, int nchunks, bool final_out) {
@@ -374,7 +384,7 @@ __device__ __forceinline__ void stage_rows(unsigned char* tiles, uint32_t t_row,
       for (int i = 0; i < 32; ++i) o[i] = 0u;
     }
     if (final_out) {
-      unsigned char* row = tiles + (c >> 1) * kOutBoxBytes + r * 128;
+      unsigned char* row = tiles + out_box_off(c >> 1) + r * 128;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         uint4 w;
@@ -386,7 +396,7 @@ __device__ __forceinline__ void stage_rows(unsigned char* tiles, uint32_t t_row,
         *reinterpret_cast<uint4*>(row + ((k ^ (r & 7)) << 4)) = w;
       }
     } else {
-      unsigned char* row = tiles + c * kOutBoxBytes + r * 128;
+      unsigned char* row = tiles + out_box_off(c) + r * 128;
 #pragma unroll
       for (int v = 0; v < 8; ++v)
         *reinterpret_cast<float4*>(row + ((v ^ (r & 7)) << 4)) =
@@ -614,14 +624,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) {
       // Q: the RoPE half into its own buffer, this CTA's 256 latent dims (four 64-dim boxes of
-      // 128 heads) into ring stages 2-3, which the QK warp copies into TMEM before its first MMA
+      // 128 heads) into the last two ring stages, which the QK warp copies into TMEM before its first MMA
       // (rows past H are zero-filled).
       mbar_arrive_expect_tx(sh.bar(kBarQFull), kQRopeBytes + kQLatBytes);
       tma_load_3d(sh.base + kOffQRope, &tm_q_rope, sh.bar(kBarQFull), 512 + kHalfRope * rank, h0, b,
                   policy_evict_last());
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tma_load_3d(sh.stage(2) + c * kQBoxBytes, &tm_q_lat, sh.bar(kBarQFull), kHalfLatent * rank + 64 * c, h0, b,
+        tma_load_3d(sh.stage(kQStage) + c * kQBoxBytes, &tm_q_lat, sh.bar(kBarQFull), kHalfLatent * rank + 64 * c, h0, b,
                     policy_evict_last());
     }
     if (ntiles > 0) {
@@ -652,7 +662,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       } else {
         if (lane == 0 && j >= kStages) ok = waiter.wait(sh.bar(kBarKvEmpty + s), ((j / kStages) - 1) & 1);
         // Stages 2 and 3 first held Q's latent half, until the QK warp copied it into TMEM.
-        if (lane == 0 && ok && j == 2) ok = waiter.wait(sh.bar(kBarQCopied), 0);
+        if (lane == 0 && ok && j == kQStage) ok = waiter.wait(sh.bar(kBarQCopied), 0);
       }
       if (lane == 0 && ok && j >= kRopeSlots) ok = waiter.wait(sh.bar(kBarRopeEmpty + rs), ((j / kRopeSlots) - 1) & 1);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -686,13 +696,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // FP8 rows: Q's latent half is converted to fp16 in place first.
       if (kFp8) ok = ok && (ntiles == 0 || waiter.wait(sh.bar(kBarQConv), 0));
       if (ok && ntiles > 0) {
-        // Q's latent half: smem (ring stages 2-3, 128B-swizzled 64-dim boxes) -> TMEM columns
+        // Q's latent half: smem (its two ring stages, 128B-swizzled 64-dim boxes) -> TMEM columns
         // kColQ + 8k for the 16-dim step k, ahead of (and in order with) the first QK.
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 16; ++k)
           tmem_cp_128x256b(tmem + kColQ + 8 * k,
-                           smem_desc(sh.stage(2) + (k >> 2) * kQBoxBytes + (k & 3) * 32, 16, 1024, kSwizzle128B));
+                           smem_desc(sh.stage(kQStage) + (k >> 2) * kQBoxBytes + (k & 3) * 32, 16, 1024, kSwizzle128B));
         mma_commit(sh.bar(kBarQCopied));
       }
       for (int j = 0; ok && j < ntiles; ++j) {
@@ -798,11 +808,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto wait_warp = [&](uint32_t bar, uint32_t parity) {
       return __all_sync(0xffffffffu, waiter.wait(bar, parity) ? 1 : 0) != 0;
     };
-    // Q's latent half (ring stages 2-3), bf16 -> fp16, before the QK warp copies it into TMEM.
+    // Q's latent half (its two ring stages), bf16 -> fp16, before the QK warp copies it into TMEM.
     if (ntiles > 0) {
       ok = wait_warp(sh.bar(kBarQFull), 0);
       if (ok && !kFp16) {
-        uint4* qs = reinterpret_cast<uint4*>(smem_gen + kOffStages + 2 * kStageBytes);
+        uint4* qs = reinterpret_cast<uint4*>(smem_gen + kOffStages + kQStage * kStageBytes);
 #pragma unroll 4
         for (int i = t; i < (int)(kQLatBytes / 16); i += 128) {
           uint4 v = qs[i];
@@ -817,9 +827,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s = j % kStages, ls = j % kLandSlots;
       if (!wait_warp(sh.bar(kBarLandFull0 + ls), (j / kLandSlots) & 1)) break;
-      // Ring stage s was last read by PV(j - kStages); stages 2-3 first held Q's latent half.
+      // Ring stage s was last read by PV(j - kStages); the last two stages first held Q's latent half.
       if (j >= kStages && !wait_warp(sh.bar(kBarKvEmpty + s), ((j / kStages) - 1) & 1)) break;
-      if (j == 2 && !wait_warp(sh.bar(kBarQCopied), 0)) break;
+      if (j == kQStage && !wait_warp(sh.bar(kBarQCopied), 0)) break;
       const uint32_t bm = land_mask[ls];
       const int nvalid = min(kTile, end - (start + j * kTile));
       const unsigned char* src = smem_gen + kOffLand + ls * kLandBytes;
@@ -1193,7 +1203,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       drain_wait(sh.bar(kBarQFull), 0, args.wait_ns);
       if (kFp8) drain_wait(sh.bar(kBarQConv), 0, args.wait_ns);
       const float l = lstat[2 * (quarter * 32 + lane)];
-      stage_rows<T>(smem_gen + kOffStages, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
+      stage_rows<T>(smem_gen, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
                     4 * wg, 4, final_out);
       fence_proxy_async_smem();
       __syncwarp();
@@ -1205,16 +1215,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (final_out) {
 #pragma unroll 1
             for (int c = 0; c < 4; ++c)
-              tma_store_3d(&tm_out, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 64 * c, h0, b);
+              tma_store_3d(&tm_out, sh.base + out_box_off(c), kHalfLatent * (int)rank + 64 * c, h0, b);
           } else if (args.units) {
 #pragma unroll 1
             for (int c = 0; c < 8; ++c)
-              tma_store_3d(&tm_part, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 32 * c, h0,
+              tma_store_3d(&tm_part, sh.base + out_box_off(c), kHalfLatent * (int)rank + 32 * c, h0,
                            slot);
           } else {
 #pragma unroll 1
             for (int c = 0; c < 8; ++c)
-              tma_store_4d(&tm_part, sh.base + kOffStages + c * kOutBoxBytes, kHalfLatent * (int)rank + 32 * c, split,
+              tma_store_4d(&tm_part, sh.base + out_box_off(c), kHalfLatent * (int)rank + 32 * c, split,
                            h0, b);
           }
           bulk_commit_group();
