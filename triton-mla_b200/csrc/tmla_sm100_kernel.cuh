@@ -106,9 +106,9 @@ using namespace ptx;
 // FP8 rows: the producer's TMA loads land in their own slots (e4m3 latent values, scales,
 // RoPE) and a fifth warpgroup dequantises each tile into the ring as fp16, the type of every
 // latent product (Q's latent half is converted once, P is written as fp16).  A ring stage
-// is then held from its dequantisation, not from its TMA issue, to the end of PV; the RoPE
-// slots are held across the dequantisation too, hence one more of them, and shared memory
-// pays for the landing slots with single score-exchange and P buffers.
+// is then held from its dequantisation, not from its TMA issue, to the end of PV (the landing
+// slots absorb the TMA latency), and shared memory pays for the landing slots with one ring
+// stage; the RoPE slots are held across the dequantisation too.
 constexpr bool kFp8 = TMLA_SM100_FP8 != 0;
 constexpr int kTile = 64;                 // tokens per pipeline stage
 constexpr int kStages = kFp8 ? 3 : 4;     // latent cache-tile ring depth (held until PV)
