@@ -198,8 +198,8 @@ def run_layer(args, cfg, device, world, rank, local):
     x = torch.randn(B, mcfg.hidden_size, generator=g, device=device, dtype=torch.bfloat16)
     splits = get_num_splits(B, 128, ctx + 1, torch.cuda.get_device_properties(device).multi_processor_count)
     # The library's launches per step: kv append (+ q_norm), the decode query's RoPE and W_UK
-    # product, W_UV, the decode (+ merge), and the projections that take the tcgen05 projection
-    # kernel ([wq_a; wkv_a], wq_b, wo).
+    # product, W_UV, the decode (+ merge), the projections that take the tcgen05 projection
+    # kernel ([wq_a; wkv_a], wq_b, wo) and the L2 prefetch beside the decode.
     from triton_mla import layer_ops
     x_rows = torch.empty(B, mcfg.hidden_size, device=device, dtype=torch.bfloat16)
     q_rows = torch.empty(B, mcfg.q_lora_rank, device=device, dtype=torch.bfloat16)
@@ -207,6 +207,9 @@ def run_layer(args, cfg, device, world, rank, local):
     layer_launches = 4 + (2 if splits > 1 else 1) + sum(
         layer_ops.linear_preferred(a, w)
         for a, w in ((x_rows, layer._w_a()), (q_rows, layer.wq_b.weight), (o_rows, layer.wo.weight)))
+    # the L2 prefetch beside the decode: W_UV, and the first part of wo when asked for
+    if layer.l2_prefetch_wo_bytes >= 0:
+        layer_launches += 1 + (layer.l2_prefetch_wo_bytes > 0)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     flops, nbytes = layer_counts(B, ctx)
