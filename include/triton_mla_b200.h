@@ -108,7 +108,11 @@ typedef struct TmlaDecodeParams {
 
   /* Split workspace (only read when num_splits > 1):
      ws_o [batch, num_heads, num_splits, d_v] fp32 partial outputs (normalised),
-     ws_lse [batch, num_heads, num_splits] fp32 base-2 partial LSE. */
+     ws_lse [batch, num_heads, num_splits] fp32 base-2 partial LSE.
+     This is the layout tmla_decode_partial writes and tmla_combine reads.  Within one
+     tmla_decode (or tmla_decode_units) call the workspace is the call's own: on the tcgen05
+     kernel the partials there are in the q dtype (16-bit, the first half of ws_o's bytes),
+     which halves what the split kernel stores and the merge reads back. */
   float* ws_o;
   float* ws_lse;
 
@@ -162,8 +166,9 @@ int tmla_decode_noalloc(const TmlaDecodeParams* p, void* stream);
 int32_t tmla_plan_units(const int32_t* seqlens, int32_t batch, int32_t num_heads, int32_t num_sms,
                         int32_t max_units, int32_t* units, int32_t* req_first);
 
-/* Workspace of a plan with num_slots partial slots: ws_o = [num_slots, num_heads, d_v] fp32 at
-   its start, ws_lse = [num_slots, num_heads] fp32 at the next 256-byte boundary. */
+/* Workspace of a plan with num_slots partial slots: room for ws_o = [num_slots, num_heads, d_v]
+   fp32 at its start (tmla_decode_units keeps its partials there in the q dtype), and
+   ws_lse = [num_slots, num_heads] fp32 at the next 256-byte boundary. */
 size_t tmla_units_workspace_bytes(int32_t num_slots, int32_t num_heads, int32_t d_v);
 
 /* Whole decode following a plan from tmla_plan_units (units and req_first copied to device

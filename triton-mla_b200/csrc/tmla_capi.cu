@@ -19,13 +19,14 @@
 
 namespace tmla {
 int launch_generic(const TmlaDecodeParams& p, cudaStream_t stream);
-int launch_combine(const float* ws_o, const float* ws_lse, void* out, int64_t osb, int64_t osh, float* lse,
-                   int64_t lsb, int B, int H, int S, int DV, int dtype, cudaStream_t stream);
+int launch_combine(const void* ws_o, const float* ws_lse, void* out, int64_t osb, int64_t osh, float* lse,
+                   int64_t lsb, int B, int H, int S, int DV, int dtype, bool part16, cudaStream_t stream);
 int sm100_supported(const TmlaDecodeParams& p);
 int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* units = nullptr,
-                 int32_t num_units = 0, int32_t num_slots = 0);
-int launch_combine_slots(const float* ws_o, const float* ws_lse, const int32_t* req_first, void* out, int64_t osb,
-                         int64_t osh, float* lse, int64_t lsb, int B, int H, int DV, int dtype, cudaStream_t stream);
+                 int32_t num_units = 0, int32_t num_slots = 0, bool part16 = false);
+int launch_combine_slots(const void* ws_o, const float* ws_lse, const int32_t* req_first, void* out, int64_t osb,
+                         int64_t osh, float* lse, int64_t lsb, int B, int H, int DV, int dtype, bool part16,
+                         cudaStream_t stream);
 }  // namespace tmla
 
 namespace {
@@ -76,10 +77,11 @@ int select_kernel(const TmlaDecodeParams& p) {
   return tmla::sm100_supported(p) ? TMLA_KERNEL_SM100 : TMLA_KERNEL_GENERIC;
 }
 
-int run_partial(const TmlaDecodeParams& p, cudaStream_t stream) {
+// part16: the tcgen05 kernel writes its split partials in the q dtype (16-bit) instead of fp32.
+int run_partial(const TmlaDecodeParams& p, cudaStream_t stream, bool part16 = false) {
   const int k = select_kernel(p);
   if (k < 0) return -k;
-  if (k == TMLA_KERNEL_SM100) return finish(tmla::launch_sm100(p, stream));
+  if (k == TMLA_KERNEL_SM100) return finish(tmla::launch_sm100(p, stream, nullptr, 0, 0, part16));
   return finish(tmla::launch_generic(p, stream));
 }
 
@@ -166,7 +168,7 @@ int tmla_combine(const float* ws_o, const float* ws_lse, void* out, int64_t out_
   if (batch == 0) return TMLA_OK;
   if (!ws_o || !ws_lse || !out) return TMLA_ERR_INVALID_ARG;
   return finish(tmla::launch_combine(ws_o, ws_lse, out, out_stride_b, out_stride_h, lse, lse_stride_b, batch,
-                                     num_heads, num_splits, d_v, dtype, static_cast<cudaStream_t>(stream)));
+                                     num_heads, num_splits, d_v, dtype, false, static_cast<cudaStream_t>(stream)));
 }
 
 int tmla_decode(const TmlaDecodeParams* p, void* stream) {
@@ -179,11 +181,15 @@ int tmla_decode(const TmlaDecodeParams* p, void* stream) {
   if (rc) return rc;
   if (q.batch == 0) return TMLA_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  rc = run_partial(q, s);
+  // Between its two stages this call owns the workspace, so the tcgen05 kernel hands the merge
+  // its partials in the q dtype (half the bytes to store and read back); the generic kernel's
+  // are fp32, and tmla_decode_partial / tmla_combine keep the documented fp32 layout.
+  const bool part16 = q.num_splits > 1 && select_kernel(q) == TMLA_KERNEL_SM100;
+  rc = run_partial(q, s, part16);
   if (rc) return rc;
-  if (p->num_splits == 1) return TMLA_OK;
-  return tmla_combine(p->ws_o, p->ws_lse, p->out, p->out_stride_b, p->out_stride_h, p->lse, p->lse_stride_b,
-                      p->batch, p->num_heads, p->num_splits, p->d_v, p->dtype, stream);
+  if (q.num_splits == 1) return TMLA_OK;
+  return finish(tmla::launch_combine(q.ws_o, q.ws_lse, q.out, q.out_stride_b, q.out_stride_h, q.lse, q.lse_stride_b,
+                                     q.batch, q.num_heads, q.num_splits, q.d_v, q.dtype, part16, s));
 }
 
 // ---------------------------------------------------------------- per-request split plan
@@ -298,10 +304,11 @@ int tmla_decode_units(const TmlaDecodeParams* p, const int32_t* units, const int
   if (num_slots > 0 && (!q.ws_o || !q.ws_lse)) return TMLA_ERR_WORKSPACE;
   if (q.kernel == TMLA_KERNEL_GENERIC || !tmla::sm100_supported(q)) return TMLA_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  rc = finish(tmla::launch_sm100(q, s, units, num_units, num_slots));
+  // The slots' partials are in the q dtype (the workspace is this call's own, as in tmla_decode).
+  rc = finish(tmla::launch_sm100(q, s, units, num_units, num_slots, true));
   if (rc || num_slots == 0) return rc;
   return finish(tmla::launch_combine_slots(q.ws_o, q.ws_lse, req_first, q.out, q.out_stride_b, q.out_stride_h, q.lse,
-                                           q.lse_stride_b, q.batch, q.num_heads, q.d_v, q.dtype, s));
+                                           q.lse_stride_b, q.batch, q.num_heads, q.d_v, q.dtype, true, s));
 }
 
 }  // extern "C"

@@ -49,30 +49,33 @@ static int encode3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, 
   return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
 }
 
-// The fp32 split partials ws_o [batch, heads, splits, 512] as a 4-D map with boxes of
-// 32 columns x 1 split x 128 heads x 1 request.
-static int encode_partials(CUtensorMap* map, float* ws_o, int batch, int heads, int splits) {
+// The split partials ws_o [batch, heads, splits, 512] as a 4-D map with boxes of 128 bytes of
+// columns (32 fp32 or 64 16-bit) x 1 split x 128 heads x 1 request.  part_dt: the element type
+// (fp32, or the q dtype when tmla_decode hands the partials to its own merge).
+static int encode_partials(CUtensorMap* map, void* ws_o, int batch, int heads, int splits, CUtensorMapDataType part_dt) {
   auto fn = encode_fn();
   if (!fn) return TMLA_ERR_CUDA;
+  const cuuint64_t e = part_dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
   cuuint64_t dims[4] = {512, (cuuint64_t)splits, (cuuint64_t)heads, (cuuint64_t)batch};
-  cuuint64_t strides[3] = {512 * 4, (cuuint64_t)splits * 512 * 4, (cuuint64_t)heads * splits * 512 * 4};
-  cuuint32_t box[4] = {32, 1, 128, 1};
+  cuuint64_t strides[3] = {512 * e, (cuuint64_t)splits * 512 * e, (cuuint64_t)heads * splits * 512 * e};
+  cuuint32_t box[4] = {(cuuint32_t)(128 / e), 1, 128, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws_o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = fn(map, part_dt, 4, ws_o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
 }
 
-// The fp32 partials of a per-request split plan, ws_o [slots, heads, 512], as a 3-D map with
-// boxes of 32 columns x 128 heads x 1 slot.
-static int encode_slot_partials(CUtensorMap* map, float* ws_o, int slots, int heads) {
+// The partials of a per-request split plan, ws_o [slots, heads, 512], as a 3-D map with boxes of
+// 128 bytes of columns x 128 heads x 1 slot (element type as for encode_partials).
+static int encode_slot_partials(CUtensorMap* map, void* ws_o, int slots, int heads, CUtensorMapDataType part_dt) {
   auto fn = encode_fn();
   if (!fn) return TMLA_ERR_CUDA;
+  const cuuint64_t e = part_dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
   cuuint64_t dims[3] = {512, (cuuint64_t)heads, (cuuint64_t)slots};
-  cuuint64_t strides[2] = {512 * 4, (cuuint64_t)heads * 512 * 4};
-  cuuint32_t box[3] = {32, 128, 1};
+  cuuint64_t strides[2] = {512 * e, (cuuint64_t)heads * 512 * e};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / e), 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ws_o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = fn(map, part_dt, 3, ws_o, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : TMLA_ERR_MISALIGNED;
 }
@@ -103,7 +106,7 @@ int sm100_supported(const TmlaDecodeParams& p) {
 }
 
 int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* units, int32_t num_units,
-                 int32_t num_slots) {
+                 int32_t num_slots, bool part16) {
   using namespace sm100;
   if (!sm100_supported(p)) return TMLA_ERR_UNSUPPORTED;
   const CUtensorMapDataType dt =
@@ -149,8 +152,9 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
     rc = encode3d(&tm_out, dt, p.out, 512, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.out_stride_h * 2,
                   (uint64_t)p.out_stride_b * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc && any_part) {
-    rc = units ? encode_slot_partials(&tm_part, p.ws_o, num_slots, p.num_heads)
-               : encode_partials(&tm_part, p.ws_o, p.batch, p.num_heads, p.num_splits);
+    const CUtensorMapDataType part_dt = part16 ? dt : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    rc = units ? encode_slot_partials(&tm_part, p.ws_o, num_slots, p.num_heads, part_dt)
+               : encode_partials(&tm_part, p.ws_o, p.batch, p.num_heads, p.num_splits, part_dt);
   }
   if (rc) return rc;
   KernelArgs a;
@@ -182,11 +186,19 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   cudaError_t e;
   if (fp8) {
     namespace v = sm100_fp8;
-    e = p.dtype == TMLA_DTYPE_FP16 ? launch(v::mla_sm100_split_kernel<__half>, v::kThreads, v::kSmemBytes)
-                                   : launch(v::mla_sm100_split_kernel<__nv_bfloat16>, v::kThreads, v::kSmemBytes);
+    if (p.dtype == TMLA_DTYPE_FP16)
+      e = part16 ? launch(v::mla_sm100_split_kernel<__half, true>, v::kThreads, v::kSmemBytes)
+                 : launch(v::mla_sm100_split_kernel<__half, false>, v::kThreads, v::kSmemBytes);
+    else
+      e = part16 ? launch(v::mla_sm100_split_kernel<__nv_bfloat16, true>, v::kThreads, v::kSmemBytes)
+                 : launch(v::mla_sm100_split_kernel<__nv_bfloat16, false>, v::kThreads, v::kSmemBytes);
   } else {
-    e = p.dtype == TMLA_DTYPE_FP16 ? launch(mla_sm100_split_kernel<__half>, kThreads, kSmemBytes)
-                                   : launch(mla_sm100_split_kernel<__nv_bfloat16>, kThreads, kSmemBytes);
+    if (p.dtype == TMLA_DTYPE_FP16)
+      e = part16 ? launch(mla_sm100_split_kernel<__half, true>, kThreads, kSmemBytes)
+                 : launch(mla_sm100_split_kernel<__half, false>, kThreads, kSmemBytes);
+    else
+      e = part16 ? launch(mla_sm100_split_kernel<__nv_bfloat16, true>, kThreads, kSmemBytes)
+                 : launch(mla_sm100_split_kernel<__nv_bfloat16, false>, kThreads, kSmemBytes);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -(int)e;

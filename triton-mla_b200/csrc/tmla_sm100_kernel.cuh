@@ -406,7 +406,8 @@ __device__ __forceinline__ void stage_rows(unsigned char* tiles, uint32_t t_row,
   }
 }
 
-template <typename T>
+// kPart16: split partials in the q dtype (tmla_decode's own merge reads them), else fp32.
+template <typename T, bool kPart16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_sm100_split_kernel(const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
                            const __grid_constant__ CUtensorMap tm_kv_scale,
@@ -1203,8 +1204,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       drain_wait(sh.bar(kBarQFull), 0, args.wait_ns);
       if (kFp8) drain_wait(sh.bar(kBarQConv), 0, args.wait_ns);
       const float l = lstat[2 * (quarter * 32 + lane)];
+      // 16-bit tiles for the final output and for 16-bit partials, fp32 tiles otherwise.
       stage_rows<T>(smem_gen, tmem + q_lanes, have_o, quarter * 32 + lane, l > 0.f ? 1.f / l : 0.f,
-                    4 * wg, 4, final_out);
+                    4 * wg, 4, final_out || kPart16);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(sh.bar(kBarEpi));
@@ -1216,6 +1218,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < 4; ++c)
               tma_store_3d(&tm_out, sh.base + out_box_off(c), kHalfLatent * (int)rank + 64 * c, h0, b);
+          } else if (kPart16) {
+            // 16-bit partials: four boxes of 64 columns, like the final output.
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              if (args.units)
+                tma_store_3d(&tm_part, sh.base + out_box_off(c), kHalfLatent * (int)rank + 64 * c, h0, slot);
+              else
+                tma_store_4d(&tm_part, sh.base + out_box_off(c), kHalfLatent * (int)rank + 64 * c, split, h0, b);
+            }
           } else if (args.units) {
 #pragma unroll 1
             for (int c = 0; c < 8; ++c)
