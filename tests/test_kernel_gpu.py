@@ -7,6 +7,8 @@ Tolerances: output max-abs <= 2e-2 and LSE max-abs <= 1e-3
 against the fp32 reference for 16-bit inputs; zero-length rows exactly 0 / -inf.
 """
 
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -944,3 +946,58 @@ def test_decode_timed_out_wait_returns_cleanly(device, rows):
     torch.cuda.synchronize()
     assert read_status(device) == 0
     check(out, lse, ref_out, ref_lse, case["seqlens"], lse_tol=lse_tol)
+
+
+def test_two_stage_c_abi_keeps_the_fp32_partial_layout(device):
+    """tmla_decode_partial writes the documented fp32 split partials (ws_o [B, H, S, 512] of
+    normalised rows, ws_lse [B, H, S] base-2) and tmla_combine merges them: the merge done here
+    in torch from those buffers, tmla_combine's result, tmla_decode's (whose tcgen05 path keeps
+    its partials in the q dtype) and the oracle all agree."""
+    import ctypes
+
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    lens, splits = [4096, 1000, 0, 65], 5
+    case = recipes.paged_case(lens, 128, 64, seed=12)
+    c = to_dev(case, device)
+    B, H = 4, 128
+    nbytes = lib.tmla_workspace_bytes(B, H, splits, 512)
+    o_bytes = (B * H * splits * 512 * 4 + 255) & ~255
+    results = {}
+    for name in ("partial", "decode"):
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        out = torch.full((B, H, 512), float("nan"), dtype=torch.bfloat16, device=device)
+        lse = torch.full((B, H), float("nan"), dtype=torch.float32, device=device)
+        p = _lib.TmlaDecodeParams(
+            c["q"].data_ptr(), c["q"].stride(0), c["q"].stride(1), c["kv"].data_ptr(), c["kv"].stride(0),
+            c["kv"].stride(1), c["kv"].shape[0], 64, c["seqlens"].data_ptr(), c["block_table"].data_ptr(),
+            c["block_table"].stride(0), c["block_table"].shape[1], out.data_ptr(), out.stride(0), out.stride(1),
+            lse.data_ptr(), lse.stride(0), ws.data_ptr(), ws.data_ptr() + o_bytes, None, B, H, 576, 512, splits,
+            _lib.DTYPE_BF16, _lib.KERNEL_AUTO, 0, case["scale"])
+        if name == "partial":
+            assert lib.tmla_decode_partial(ctypes.byref(p), stream) == 0
+            torch.cuda.synchronize(device)
+            ws_o = ws[: B * H * splits * 512 * 4].view(torch.float32).view(B, H, splits, 512).clone()
+            ws_lse = ws[o_bytes: o_bytes + B * H * splits * 4].view(torch.float32).view(B, H, splits).clone()
+            assert lib.tmla_combine(ctypes.c_void_p(p.ws_o), ctypes.c_void_p(p.ws_lse), ctypes.c_void_p(out.data_ptr()),
+                                    out.stride(0), out.stride(1), ctypes.c_void_p(lse.data_ptr()), lse.stride(0),
+                                    B, H, splits, 512, _lib.DTYPE_BF16, stream) == 0
+            # The same merge in torch from the fp32 buffers.
+            m = ws_lse.amax(-1, keepdim=True)
+            m = torch.where(torch.isneginf(m), torch.zeros_like(m), m)
+            w = torch.exp2(ws_lse - m)
+            wsum = w.sum(-1)
+            t_out = (w[..., None] * torch.nan_to_num(ws_o)).sum(-2) / wsum.clamp_min(1e-30)[..., None]
+            t_lse = torch.where(wsum > 0, (m[..., 0] + torch.log2(wsum)) * math.log(2.0),
+                                torch.full_like(wsum, float("-inf")))
+            results["torch"] = (t_out, t_lse)
+        else:
+            assert lib.tmla_decode(ctypes.byref(p), stream) == 0
+        torch.cuda.synchronize(device)
+        results[name] = (out, lse)
+    ref_out, ref_lse = oracle_of(case)
+    for name, (o, l) in results.items():
+        check(o, l, ref_out, ref_lse, lens)
+    assert (results["torch"][0] - results["partial"][0].float()).abs().max().item() <= OUT_TOL
+    valid = torch.tensor(lens, device=device) > 0
+    assert (results["torch"][1][valid] - results["partial"][1][valid]).abs().max().item() <= 1e-4
