@@ -118,10 +118,8 @@ size_t tmla_workspace_bytes(int32_t batch, int32_t num_heads, int32_t num_splits
 // B200 split rule.  One unit of work is a 2-CTA cluster (the tcgen05 kernel's
 // 128-head tile of one request's split); 148 SMs run 74 such units per wave.
 // The estimate, in units of "one cluster streaming one cache row", is
-//   waves(s) * (rows per split + fixed cost per unit) + merge traffic(s)
-// where the merge traffic (fp32 partials written then read back, 2 x 4 bytes
-// x 512 columns per head and split) is spread over all clusters.  The
-// smallest split count within 2% of the best estimate wins.
+//   waves(s) * (rows per split + fixed cost per unit) + s * merge cost per split
+// (below).  The smallest split count within 2% of the best estimate wins.
 int32_t tmla_num_splits(int32_t batch, int32_t num_heads, int32_t max_seqlen, int32_t num_sms) {
   if (batch <= 0 || num_heads <= 0 || max_seqlen <= 0) return 1;
   if (num_sms <= 0) num_sms = 148;
@@ -130,7 +128,11 @@ int32_t tmla_num_splits(int32_t batch, int32_t num_heads, int32_t max_seqlen, in
   const int tiles = (max_seqlen + 63) / 64;
   const int max_s = tiles < 64 ? tiles : 64;
   const double fixed_rows = 256.0;
-  const double merge_rows_per_split = (double)batch * num_heads * 512.0 * 8.0 / (clusters * 1152.0);
+  // The merge, in cache rows streamed by one cluster, per split: the 16-bit partials the split
+  // writes (2 bytes per output element; the merge reads them back from L2 while the split
+  // kernel drains) spread over all clusters, plus 8 rows of merge latency.  Fitted to B200
+  // call times of uniform batches (1-256 requests of 1024-16384 tokens, every split count).
+  const double merge_rows_per_split = (double)batch * num_heads * 512.0 * 2.0 / (clusters * 1152.0) + 8.0;
   double cost[65];
   double best = INFINITY;
   for (int s = 1; s <= max_s; ++s) {

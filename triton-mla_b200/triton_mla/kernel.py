@@ -155,7 +155,7 @@ def _num_splits_rule(batch, num_heads, max_seqlen, num_sms):
     clusters = max(num_sms // 2, 1)
     units = batch * ((num_heads + 127) // 128)
     tiles = (max_seqlen + 63) // 64
-    merge = batch * num_heads * 512.0 * 8.0 / (clusters * 1152.0)
+    merge = batch * num_heads * 512.0 * 2.0 / (clusters * 1152.0) + 8.0
     cost = {}
     for s in range(1, min(tiles, 64) + 1):
         waves = (units * s + clusters - 1) // clusters
@@ -170,9 +170,9 @@ def get_num_splits(batch, num_heads, max_seqlen, num_sms, min_tokens_per_split=1
     Replaces the reference's one-wave power-of-two rule (kernel.py:190-201).
     The tcgen05 kernel runs one 2-SM cluster per (request, 128-head tile,
     split), so a 148-SM B200 holds 74 of them per wave; the C library picks the
-    count that minimises waves x (rows per split + fixed cost) + the fp32
-    partial traffic of the merge.  ``min_tokens_per_split`` caps the count as
-    in the reference.
+    count that minimises waves x (rows per split + fixed cost) + the merge's
+    cost per split (the 16-bit partials written, plus a fixed latency).
+    ``min_tokens_per_split`` caps the count as in the reference.
     """
     if batch <= 0 or max_seqlen <= 0:
         return 1
