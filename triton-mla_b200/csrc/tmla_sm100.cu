@@ -144,8 +144,8 @@ int launch_sm100(const TmlaDecodeParams& p, cudaStream_t stream, const int32_t* 
   if (!rc)
     rc = encode3d(&tm_qlat, dt, p.q, 576, (uint64_t)p.num_heads, (uint64_t)p.batch, (uint64_t)p.q_stride_h * 2,
                   (uint64_t)p.q_stride_b * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-  // The final 16-bit output (one split) and the fp32 partials (several) as tensor maps;
-  // a plan of per-request splits can need both in one launch.
+  // The final 16-bit output (one split) and the partials (several; fp32, or 16-bit with
+  // part16) as tensor maps; a plan of per-request splits can need both in one launch.
   const bool any_final = units ? num_slots < num_units : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
   const bool any_part = units ? num_slots > 0 : !any_final;
   if (!rc && any_final)

@@ -58,8 +58,8 @@
 // first tile (page ids read speculatively at entry) and Q's RoPE half are
 // requested before the CTA-wide and cluster-wide syncs.  Epilogue: warpgroups A
 // and B stage O (scaled by 1/l) into 128B-swizzled tiles in the idle cache ring
-// and one thread writes them with TMA tensor stores (fp32 split partials, or the
-// final 16-bit output; rows past H lie outside the tensor map and are skipped).
+// and one thread writes them with TMA tensor stores (split partials in fp32 or 16-bit,
+// or the final 16-bit output; rows past H lie outside the tensor map and are skipped).
 //
 // Every wait is bounded (2 s per wait, %globaltimer); on expiry the CTA sets
 // TMLA_STATUS_TIMEOUT, all roles leave their loops, in-flight copies and MMAs
@@ -161,7 +161,7 @@ constexpr uint32_t kOffStat = kOffRope + kFinBytes;
 static_assert(kFinBytes + kStatBytes <= kRopeSlots * kRopeBytes, "epilogue scratch must fit in the RoPE ring");
 static_assert(kOffPBuf % 1024 == 0 && kOffSin % 1024 == 0,
               "P buffers and epilogue tiles must be 1024-byte aligned for the 128-byte swizzle");
-// Epilogue tiles (8 of 16 KB for fp32 partials, 4 for the final output) reuse the cache-tile
+// Epilogue tiles (8 of 16 KB for fp32 partials, 4 for 16-bit ones) reuse the cache-tile
 // ring and, past its end, the score-exchange buffers.
 static_assert(kStages * kStageBytes + kSinBufs * kSinBytes >= 8 * 128 * 128, "no room for the epilogue tiles");
 constexpr uint32_t kNumBars = 2 * kStages + kRopeSlots + 40;
@@ -451,7 +451,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (un.x < 0) return;
     b = un.x, split = un.y, nsplit = un.z, slot = un.w;
   }
-  // One split writes the final output (and natural-log LSE); several write fp32 partials.
+  // One split writes the final output (and natural-log LSE); several write partials.
   const bool final_out = args.units ? nsplit == 1 : (p.num_splits == 1 && !(p.flags & TMLA_FLAG_PARTIAL_ONLY));
   const int H = p.num_heads;
   const Waiter waiter{abort_flag, p.status, args.wait_ns, map_to_rank(sh.base + kOffMisc, peer)};
