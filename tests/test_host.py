@@ -120,6 +120,22 @@ def test_num_splits_b200_configs():
     assert get_num_splits(0, 128, 4096, 148) == 1
 
 
+@pytest.mark.parametrize("batch,seqlen,want", [
+    (32, 4096, 2),     # config 2
+    (4, 65536, 18),    # config 3
+    (16, 8192, 4),     # config 5's decode
+    (4, 4096, 16),     # a rank's share of config 2 at N = 8
+    (1, 1024, 8),
+    (24, 1024, 3),
+    (128, 16384, 4),
+    (256, 8192, 2),
+])
+def test_num_splits_matches_the_measured_choices(batch, seqlen, want):
+    # The split counts the rule gives for shapes whose call times were measured on a B200
+    # (each the fastest count measured, or within 0.13% of it).
+    assert get_num_splits(batch, 128, seqlen, 148) == want
+
+
 def test_wrapper_assertions_match_reference():
     q = torch.zeros(2, 16, 576, dtype=torch.bfloat16)
     kv = torch.zeros(2, 64, 576, dtype=torch.bfloat16)
