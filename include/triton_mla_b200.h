@@ -43,6 +43,9 @@ extern "C" {
 #define TMLA_ERR_CUDA 4            /* a CUDA runtime/driver call failed; see tmla_last_cuda_error() */
 #define TMLA_ERR_WORKSPACE 5       /* workspace missing or too small */
 
+/* Largest batch and split count of one decode call (a grid dimension's limit). */
+#define TMLA_MAX_BATCH 65535
+
 /* Bits of the device status word (OR-ed by kernels). */
 #define TMLA_STATUS_BAD_PAGE 0x1   /* a block-table entry was outside [0, num_pages); its tokens were masked */
 #define TMLA_STATUS_TIMEOUT 0x2    /* a bounded pipeline wait gave up; the result is invalid */
@@ -118,6 +121,8 @@ typedef struct TmlaDecodeParams {
 
   int32_t* status;                 /* optional device status word (TMLA_STATUS_* bits), or NULL */
 
+  /* batch and num_splits are at most TMLA_MAX_BATCH: larger values give TMLA_ERR_UNSUPPORTED
+     (decode such a batch as several calls).  The reference's Triton grid has no such limit. */
   int32_t batch, num_heads, d_qk, d_v, num_splits;
   int32_t dtype;                   /* TMLA_DTYPE_* */
   int32_t kernel;                  /* TMLA_KERNEL_* */

@@ -47,7 +47,7 @@ def test_abi_version_and_struct_layout():
     text = HEADER.read_text()
     for name in ("OK", "ERR_INVALID_ARG", "ERR_UNSUPPORTED", "ERR_MISALIGNED", "ERR_CUDA", "ERR_WORKSPACE",
                  "STATUS_BAD_PAGE", "STATUS_TIMEOUT", "STATUS_RANGE", "DTYPE_BF16", "DTYPE_FP16", "DTYPE_FP32", "KERNEL_AUTO",
-                 "KERNEL_GENERIC", "KERNEL_SM100", "FLAG_PARTIAL_ONLY"):
+                 "KERNEL_GENERIC", "KERNEL_SM100", "FLAG_PARTIAL_ONLY", "MAX_BATCH"):
         m = re.search(rf"#define TMLA_{name}\s+(0x[0-9a-fA-F]+|\d+)", text)
         assert m and int(m.group(1), 0) == getattr(_lib, name), name
 
@@ -80,6 +80,18 @@ def _params(**kw):
 def test_select_kernel_rejects_invalid(bad):
     rc = _lib.load().tmla_select_kernel(ctypes.byref(_params(**bad)))
     assert rc == -_lib.ERR_INVALID_ARG
+
+
+def test_batches_beyond_the_grid_limit_are_refused():
+    # One decode call covers at most TMLA_MAX_BATCH requests and splits (a grid dimension's
+    # limit); beyond it the call is refused before any launch.
+    lib = _lib.load()
+    big = dict(batch=_lib.MAX_BATCH + 1, num_pages=10)
+    assert lib.tmla_select_kernel(ctypes.byref(_params(**big))) == -_lib.ERR_UNSUPPORTED
+    assert lib.tmla_decode(ctypes.byref(_params(**big)), None) == _lib.ERR_UNSUPPORTED
+    ws = dict(num_splits=_lib.MAX_BATCH + 1, ws_o=16, ws_lse=16)
+    assert lib.tmla_select_kernel(ctypes.byref(_params(**ws))) == -_lib.ERR_UNSUPPORTED
+    assert lib.tmla_select_kernel(ctypes.byref(_params(batch=_lib.MAX_BATCH))) >= 0
 
 
 def test_select_kernel_needs_workspace_for_splits():

@@ -50,6 +50,8 @@ bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 int validate(const TmlaDecodeParams* p) {
   if (!p) return TMLA_ERR_INVALID_ARG;
   if (p->batch < 0 || p->num_heads <= 0 || p->num_splits <= 0) return TMLA_ERR_INVALID_ARG;
+  // The kernels' grids index requests and splits in grid dimensions of at most 65535 blocks.
+  if (p->batch > TMLA_MAX_BATCH || p->num_splits > TMLA_MAX_BATCH) return TMLA_ERR_UNSUPPORTED;
   if (p->d_v <= 0 || p->d_qk <= p->d_v) return TMLA_ERR_INVALID_ARG;
   if (!is_pow2(p->d_v) || !is_pow2(p->d_qk - p->d_v)) return TMLA_ERR_INVALID_ARG;
   if (p->dtype != TMLA_DTYPE_BF16 && p->dtype != TMLA_DTYPE_FP16 && p->dtype != TMLA_DTYPE_FP32)

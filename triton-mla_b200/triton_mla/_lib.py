@@ -23,6 +23,7 @@ ERR_UNSUPPORTED = 2
 ERR_MISALIGNED = 3
 ERR_CUDA = 4
 ERR_WORKSPACE = 5
+MAX_BATCH = 65535  # requests (and splits) of one decode call
 LAYER_FLAG_PDL = 1
 LINEAR_FLAG_TEST_STALL = 0x100
 LINEAR_MAX_TILES = 65536
