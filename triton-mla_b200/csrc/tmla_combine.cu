@@ -77,10 +77,12 @@ __device__ __forceinline__ float ld1(const P* p) {
 // Vector path (d_v a multiple of 128, at most 64 splits): one warp per (row, group of
 // 128 columns); lane l owns columns 4l..4l+3 of the group.  The split weights sit in
 // two registers per lane (splits l and l + 32) and are broadcast by shuffles, and the
-// loads of 8 splits are issued before their FMAs, so a row costs S/8 memory round
-// trips instead of S.
-template <typename T, typename P>
-__global__ void __launch_bounds__(kCombineWarps * 32, 4)
+// loads of kVecLoads splits are issued before their FMAs, so a row costs S/kVecLoads memory
+// round trips instead of S.  Sixteen loads in flight need the registers of 2 blocks per SM,
+// eight fit 4: the launch takes 16 when there are more than 8 splits and the grid still fits
+// one wave at 2 blocks per SM.
+template <typename T, typename P, int kVecLoads>
+__global__ void __launch_bounds__(kCombineWarps * 32, kVecLoads > 8 ? 2 : 4)
     mla_combine_vec_kernel(const P* __restrict__ ws_o, const float* __restrict__ ws_lse, T* __restrict__ out,
                            int64_t osb, int64_t osh, float* __restrict__ lse, int64_t lsb, int B, int H, int S,
                            int DV) {
@@ -97,11 +99,11 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 4)
   const float* L = ws_lse + row * S;
   const P* src = ws_o + row * (int64_t)S * DV + grp * 128 + 4 * lane;
   const int64_t sstride = DV;
-  // The first 8 splits' partials are requested before the LSEs have come back: the two
-  // loads do not depend on each other.
-  float4 v[8];
+  // The first kVecLoads splits' partials are requested before the LSEs have come back: the
+  // two loads do not depend on each other.
+  float4 v[kVecLoads];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) v[u] = (u < S) ? ld4<P>(src + u * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int u = 0; u < kVecLoads; ++u) v[u] = (u < S) ? ld4<P>(src + u * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
 
   const float l0 = lane < S ? L[lane] : -INFINITY, l1 = lane + 32 < S ? L[lane + 32] : -INFINITY;
   float m = fmaxf(l0, l1);
@@ -114,16 +116,16 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 4)
   for (int o = 16; o >= 1; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
 
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < S; s0 += 8) {
-    float w[8];
+  for (int s0 = 0; s0 < S; s0 += kVecLoads) {
+    float w[kVecLoads];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < kVecLoads; ++u) {
       const int s = s0 + u;
       w[u] = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
       if (s0 > 0) v[u] = (s < S) ? ld4<P>(src + s * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < kVecLoads; ++u) {
       acc.x = fmaf(w[u], v[u].x, acc.x);
       acc.y = fmaf(w[u], v[u].y, acc.y);
       acc.z = fmaf(w[u], v[u].z, acc.z);
@@ -328,8 +330,14 @@ static int launch_combine_t(const void* ws_o_v, const float* ws_lse, void* out, 
     e = cudaLaunchKernelEx(&cfg, mla_combine_row512_kernel<T, P>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S);
   } else if (vec_ok) {
     const int64_t warps = rows * (DV / 128);
-    cfg.gridDim = dim3((unsigned)((warps + kCombineWarps - 1) / kCombineWarps));
-    e = cudaLaunchKernelEx(&cfg, mla_combine_vec_kernel<T, P>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
+    const int64_t blocks = (warps + kCombineWarps - 1) / kCombineWarps;
+    cfg.gridDim = dim3((unsigned)blocks);
+    int dev = 0, sms = 0;
+    if (S > 8 && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && blocks <= 2 * (int64_t)sms)
+      e = cudaLaunchKernelEx(&cfg, mla_combine_vec_kernel<T, P, 16>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
+    else
+      e = cudaLaunchKernelEx(&cfg, mla_combine_vec_kernel<T, P, 8>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
   } else {
     cfg.gridDim = dim3((unsigned)((rows + kCombineWarps - 1) / kCombineWarps));
     e = cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, P>, ws_o, ws_lse, o, osb, osh, lse, lsb, B, H, S, DV);
